@@ -1,0 +1,172 @@
+/*
+ * C ABI of the B200-native folded-VPP prefill kernels (sm_100a).
+ *
+ * Every entry point takes device pointers, sizes and strides, enqueues on the
+ * given stream and returns a cudaError_t value (0 = success); invalid
+ * arguments return cudaErrorInvalidValue (1) before anything is launched.
+ * Device-detected problems are never a trap: kernels OR a code into the
+ * optional `status` word (QI_STATUS_* below), which the caller reads back.
+ *
+ * Interfaces replaced (paths inside the reference project,
+ * Nicko-F/qwen3.8-sm120-vpp-bucket-attention):
+ *   nvfp4_norm_pack_launch / _metadata  <- src/qwen_infra/kernels/nvfp4_norm_pack.cu:68-85
+ *   nvfp4_attention_front / _resources  <- src/qwen_infra/kernels/nvfp4_attention_front.cu:12-23,114-127
+ *   qi_norm_pack          generalises nvfp4_norm_pack_launch (any H % 64 == 0, optional residual)
+ *   qi_rms_norm           final norm of the last virtual stage (vpp/model.py:112-114)
+ *   qi_qk_rope_kv_append  generalises nvfp4_attention_front (D in {64,128,256}, status word)
+ *   qi_gate_fp8           store_final_fp8, src/qwen_infra/kernels/nvfp4_bucket_xqa.cu:48-66,
+ *                         with a per-token scale
+ *   qi_gemm               FlashInfer mm_fp4 called at src/qwen_infra/vpp/producer.py:29-45,
+ *                         vLLM scaled_fp4_quant at producer.py:200-206 (fused epilogue),
+ *                         and the FP8 O projection (kernels/nvfp4_attention_fusion.py:46)
+ *   qi_kv_dequant +
+ *   qi_prefill_attention  FlashInfer paged prefill attention selected at src/qwen_infra/config.py:80
+ *   qi_nvfp4_quantize / qi_fp8_quantize_rows  weight preparation (checkpoint NVFP4 / FP8 layouts)
+ */
+#ifndef QWEN_INFRA_B200_H
+#define QWEN_INFRA_B200_H
+
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QI_STATUS_BAD_KV_SCALE 1
+#define QI_STATUS_WAIT_TIMEOUT 2
+#define QI_STATUS_BAD_SLOT 4
+
+/* ---- fused residual + RMSNorm -> NVFP4 --------------------------------- */
+
+/* Reference ABI (nvfp4_norm_pack.cu:68): H = 5120, Gemma (1+w), eps 1e-6.
+ * x, r, updated: bf16 [rows, 5120]; w: bf16 [5120]; global: fp32 device
+ * scalar; q: u8 [rows, 2560]; scale: u8 [ceil(rows/128)*128, 320] swizzled. */
+int nvfp4_norm_pack_launch(const void* x, const void* r, const void* w, const void* global, void* q,
+                           void* scale, void* updated, int rows, cudaStream_t stream);
+int nvfp4_norm_pack_metadata(int* out); /* out[3]: registers, static smem, local bytes */
+
+/* Any hidden % 64 == 0 (<= 16384).  residual may be NULL (first layer);
+ * updated may be NULL.  weight_offset = 1 for the Gemma (1+w) form, 0 for w. */
+int qi_norm_pack(const void* x, const void* residual, const void* gamma, const float* global_scale, void* q,
+                 void* scales, void* updated, int rows, int hidden, float eps, float weight_offset,
+                 cudaStream_t stream);
+
+/* Same norm, bf16 normalised output [rows, hidden]. */
+int qi_rms_norm(const void* x, const void* residual, const void* gamma, void* out, void* updated, int rows,
+                int hidden, float eps, float weight_offset, cudaStream_t stream);
+
+/* ---- QK-norm + RoPE + gate split + NVFP4 paged KV append --------------- */
+
+/* Byte-for-byte the reference's parameter struct (nvfp4_attention_front.cu:12-23). */
+typedef struct RefFront {
+  const void *qkv, *qw, *kw;
+  const void *cos_sin, *positions, *slots;
+  const float *k_scale, *v_scale;
+  uint8_t *k, *v, *ks, *vs;
+  void *q, *gate;
+  int rows, qheads, kvheads, rotary, slot_rows, pages, page_size;
+  int cos_float, pos_long, slot_long, mrope_h, mrope_w;
+  int64_t input_row, cos_row, pos_m, pos_t;
+  int64_t data_page, data_row, data_head, sf_page, sf_row, sf_head;
+  float epsilon;
+} RefFront;
+
+/* Reference ABI: head_dim 256, rotary == 256 (MRoPE sections rejected). */
+int nvfp4_attention_front(RefFront p, cudaStream_t stream);
+int nvfp4_attention_front_resources(int* out); /* sizeof, regs, smem, local, occupancy */
+
+/* qkv row: per Q head [q(D) | gate(D)], then K heads, then V heads (bf16).
+ * cos_sin [maxpos, D]: cos in [0, D/2), sin in [D/2, D).  Caches:
+ * data [pages, page_size, Hkv, D/2] u8 and scales [.., D/16] E4M3 addressed
+ * through the strides below (bytes).  k_global / v_global are the fp32
+ * dequantisation multipliers: scale = e4m3(amax / (6 g)). */
+typedef struct QiFront {
+  const void *qkv, *q_weight, *k_weight, *cos_sin, *positions, *slots;
+  const float *k_global, *v_global;
+  void *k_cache, *v_cache, *k_scales, *v_scales, *q, *gate;
+  int* status;
+  int rows, qheads, kvheads, head_dim, slot_rows, pages, page_size;
+  int cos_float, pos_long, slot_long;
+  int64_t input_row, cos_row, q_row, gate_row;
+  int64_t data_page, data_row, data_head, sf_page, sf_row, sf_head;
+  float eps, weight_offset;
+} QiFront;
+
+int qi_qk_rope_kv_append(const QiFront* p, cudaStream_t stream);
+int qi_qk_rope_kv_append_resources(int* out);
+
+/* ---- attention output x sigmoid(gate) -> FP8 (per-token scale) --------- */
+int qi_gate_fp8(const void* out, const void* gate, int64_t out_row, int64_t gate_row, void* fp8, int64_t fp8_row,
+                float* scale, int rows, int cols, cudaStream_t stream);
+
+/* ---- tcgen05 GEMM: D[m, n] = A[m, k] . B[n, k]^T ------------------------ */
+#define QI_GEMM_NVFP4 0 /* kind::mxf4nvf4, E2M1 with 16-element E4M3 block scales */
+#define QI_GEMM_E4M3 1  /* kind::f8f6f4, E4M3 x E4M3 */
+
+#define QI_EPI_BF16 0          /* out bf16 = acc * alpha */
+#define QI_EPI_F32 1           /* out fp32 = acc * alpha */
+#define QI_EPI_SWIGLU_NVFP4 2  /* 256-col tile = 128 gate + 128 up cols -> NVFP4 act */
+#define QI_EPI_BF16_ROWCOL 3   /* out bf16 = acc * row_scale[m] * col_scale[n] */
+
+typedef struct QiGemm {
+  int kind, epilogue;
+  int m, n, k; /* k in elements; n % 256 == 0; k % 256 == 0 (NVFP4) / % 128 (E4M3) */
+  const void *a, *b;     /* row-major, K contiguous; NVFP4 packs two codes per byte */
+  const void *sfa, *sfb; /* swizzled block scales of A and B (NVFP4) */
+  const float* alpha;    /* device scalar, or NULL to use alpha_value */
+  float alpha_value;
+  const float *row_scale, *col_scale;
+  void* out;
+  int64_t ldo; /* elements */
+  void *act_q, *act_sf;  /* QI_EPI_SWIGLU_NVFP4: [m, n/4] bytes and swizzled scales of K = n/2 */
+  const float* act_global;
+  int64_t act_ld; /* bytes */
+  int* status;
+} QiGemm;
+
+int qi_gemm(const QiGemm* g, cudaStream_t stream);
+int qi_gemm_resources(int* out); /* dynamic smem bytes, regs, threads */
+
+/* ---- paged NVFP4 KV -> bf16 K / V^T and causal GQA prefill attention ---- */
+typedef struct QiKvView {
+  const void *k_cache, *v_cache, *k_scales, *v_scales;
+  int kvheads, head_dim, page_size;
+  int64_t data_page, data_row, data_head, sf_page, sf_row, sf_head;
+} QiKvView;
+
+/* k_out bf16 [Hkv, tokens, D]; vt_out bf16 [Hkv, D, vt_row] (vt_row % 64 == 0). */
+int qi_kv_dequant(const QiKvView* kv, const int32_t* block_table, int tokens, void* k_out, void* vt_out,
+                  int64_t vt_row, cudaStream_t stream);
+
+typedef struct QiAttention {
+  const void* q;         /* bf16 [rows, Hq*D] (row stride q_row elements) */
+  const void* k;         /* bf16 [Hkv, kv_tokens, D] */
+  const void* vt;        /* bf16 [Hkv, D, vt_row] */
+  void* out;             /* bf16 [rows, Hq*D] (row stride out_row) */
+  const float *k_global, *v_global;
+  int* status;
+  int rows, history, kv_tokens, qheads, kvheads, head_dim;
+  int64_t q_row, out_row, vt_row;
+  float softmax_scale;
+} QiAttention;
+
+int qi_prefill_attention(const QiAttention* p, cudaStream_t stream);
+
+/* ---- weight preparation ------------------------------------------------- */
+int qi_nvfp4_quantize(const float* w, int64_t rows, int k, const float* global_scale, void* q, void* scales,
+                      cudaStream_t stream);
+int qi_fp8_quantize_rows(const float* w, int rows, int k, void* q, float* scales, cudaStream_t stream);
+
+/* Conversion probe (tests): e2m1_pairs gets n/2 bytes packed pairwise and then
+ * n/2 bytes packed eight at a time; e4m3[n]; ex[2n] = (fexp, sigmoid) pairs. */
+int qi_convert_probe(const float* in, void* e2m1_pairs, void* e4m3, float* ex, int n, cudaStream_t stream);
+
+/* Host-only: sizeof(RefFront, QiFront, QiGemm, QiKvView, QiAttention) for ABI checks. */
+int qi_abi_struct_sizes(int* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QWEN_INFRA_B200_H */

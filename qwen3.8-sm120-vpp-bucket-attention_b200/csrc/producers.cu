@@ -1,0 +1,615 @@
+// HBM-bound producers of one decoder layer (sm_100a):
+//   * residual add + RMSNorm -> NVFP4 pack with 128x4-swizzled E4M3 scales,
+//   * the same norm with a bf16 output (final norm of the last stage),
+//   * QK-norm + NeoX RoPE + gate split + NVFP4 paged KV append,
+//   * attention output x sigmoid(gate) -> FP8 E4M3 with a per-token scale,
+//   * weight quantisers (NVFP4 per 16 + global, FP8 per output channel),
+//   * paged NVFP4 KV -> contiguous bf16 K and transposed V for attention.
+// Every fp32 step is an explicitly rounded IEEE operation; the reduction trees
+// are fixed, so the CPU restatement reproduces the quantised bytes exactly.
+#include "common.cuh"
+#include "qwen_infra_b200.h"
+
+using namespace qi;
+
+namespace {
+
+struct alignas(16) BF8 {
+  __nv_bfloat162 v[4];
+};
+
+QI_DEV void load16_bf16(const __nv_bfloat16* p, float* out) {
+  const uint4 a = reinterpret_cast<const uint4*>(p)[0];
+  const uint4 b = reinterpret_cast<const uint4*>(p)[1];
+  const __nv_bfloat162* pa = reinterpret_cast<const __nv_bfloat162*>(&a);
+  const __nv_bfloat162* pb = reinterpret_cast<const __nv_bfloat162*>(&b);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 fa = __bfloat1622float2(pa[i]);
+    float2 fb = __bfloat1622float2(pb[i]);
+    out[2 * i] = fa.x;
+    out[2 * i + 1] = fa.y;
+    out[8 + 2 * i] = fb.x;
+    out[8 + 2 * i + 1] = fb.y;
+  }
+}
+
+QI_DEV void store16_bf16(__nv_bfloat16* p, const float* v) {
+  uint4 a, b;
+  __nv_bfloat162* pa = reinterpret_cast<__nv_bfloat162*>(&a);
+  __nv_bfloat162* pb = reinterpret_cast<__nv_bfloat162*>(&b);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    pa[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    pb[i] = __floats2bfloat162_rn(v[8 + 2 * i], v[8 + 2 * i + 1]);
+  }
+  reinterpret_cast<uint4*>(p)[0] = a;
+  reinterpret_cast<uint4*>(p)[1] = b;
+}
+
+// Block-wide sum over per-thread partials: warp xor-butterfly, then a second
+// butterfly over the zero-padded per-warp sums.  Result broadcast to all.
+QI_DEV float block_sum(float v, float* scratch32) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = (blockDim.x + 31) >> 5;
+  v = warp_sum_butterfly(v);
+  if (lane == 0) scratch32[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    float w = lane < nwarps ? scratch32[lane] : 0.0f;
+    w = warp_sum_butterfly(w);
+    if (lane == 0) scratch32[32] = w;
+  }
+  __syncthreads();
+  return scratch32[32];
+}
+
+QI_DEV float block_max(float v, float* scratch32) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = (blockDim.x + 31) >> 5;
+  v = warp_max_butterfly(v);
+  if (lane == 0) scratch32[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    float w = lane < nwarps ? scratch32[lane] : 0.0f;
+    w = warp_max_butterfly(w);
+    if (lane == 0) scratch32[32] = w;
+  }
+  __syncthreads();
+  return scratch32[32];
+}
+
+// One CTA per row, thread t owns elements [16t, 16t+16) (= scale group t).
+template <bool kQuant>
+__global__ void norm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ residual,
+                            const __nv_bfloat16* __restrict__ gamma, const float* __restrict__ gscale,
+                            uint8_t* __restrict__ q, uint8_t* __restrict__ sf, __nv_bfloat16* __restrict__ updated,
+                            __nv_bfloat16* __restrict__ y_out, int hidden, float eps, float woff) {
+  __shared__ float scratch[33];
+  const int64_t row = blockIdx.x;
+  const int t = threadIdx.x;
+  const int groups = hidden >> 4;
+  const bool active = t < groups;
+  float h[16];
+  float ss = 0.0f;
+  if (active) {
+    const int64_t base = row * hidden + 16 * t;
+    load16_bf16(x + base, h);
+    if (residual) {
+      float r[16];
+      load16_bf16(residual + base, r);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) h[j] = __fadd_rn(h[j], r[j]);
+    }
+    ss = __fmul_rn(h[0], h[0]);
+#pragma unroll
+    for (int j = 1; j < 16; ++j) ss = __fadd_rn(ss, __fmul_rn(h[j], h[j]));
+    if (updated) store16_bf16(updated + base, h);
+  }
+  const float total = block_sum(ss, scratch);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)hidden), eps)));
+  if (!active) return;
+  float w[16], y[16];
+  load16_bf16(gamma + 16 * t, w);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) y[j] = bf16r(__fmul_rn(__fmul_rn(h[j], inv), __fadd_rn(w[j], woff)));
+  if constexpr (kQuant) {
+    uint2 packed;
+    const uint32_t code = nvfp4_quant16(y, *gscale, packed);
+    reinterpret_cast<uint2*>(q + row * (hidden >> 1))[t] = packed;
+    const int64_t gp = (groups + 3) & ~3;
+    sf[sf_offset(row, t, gp)] = (uint8_t)code;
+  } else {
+    store16_bf16(y_out + row * hidden + 16 * t, y);
+  }
+}
+
+// QK-norm + RoPE + gate split + NVFP4 paged append.  One warp per (row, head):
+// lane l owns E2 = D/64 consecutive elements of each rotary half.
+template <int E2>
+__global__ void __launch_bounds__(256) front_kernel(QiFront p) {
+  constexpr int D = E2 * 64, HALF = D / 2;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = blockIdx.x;
+  const int head = blockIdx.y * 8 + warp;
+  if (head >= p.qheads + p.kvheads) return;
+  const bool is_k = head >= p.qheads;
+  const int local = is_k ? head - p.qheads : head;
+  const __nv_bfloat16* qkv = static_cast<const __nv_bfloat16*>(p.qkv);
+  const int64_t base = row * p.input_row + (is_k ? (int64_t)p.qheads * 2 * D + (int64_t)local * D : (int64_t)local * 2 * D);
+  const int d0 = lane * E2;
+  float x[E2], y[E2];
+#pragma unroll
+  for (int i = 0; i < E2; ++i) {
+    x[i] = __bfloat162float(qkv[base + d0 + i]);
+    y[i] = __bfloat162float(qkv[base + HALF + d0 + i]);
+  }
+  float ss = __fmul_rn(x[0], x[0]);
+  ss = __fadd_rn(ss, __fmul_rn(y[0], y[0]));
+#pragma unroll
+  for (int i = 1; i < E2; ++i) {
+    ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));
+    ss = __fadd_rn(ss, __fmul_rn(y[i], y[i]));
+  }
+  ss = warp_sum_butterfly(ss);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), p.eps)));
+  const __nv_bfloat16* w = static_cast<const __nv_bfloat16*>(is_k ? p.k_weight : p.q_weight);
+  const int64_t pos = p.pos_long ? static_cast<const int64_t*>(p.positions)[row]
+                                 : static_cast<const int32_t*>(p.positions)[row];
+#pragma unroll
+  for (int i = 0; i < E2; ++i) {
+    const float a = bf16r(__fmul_rn(__fmul_rn(x[i], inv), __fadd_rn(__bfloat162float(w[d0 + i]), p.weight_offset)));
+    const float b =
+        bf16r(__fmul_rn(__fmul_rn(y[i], inv), __fadd_rn(__bfloat162float(w[HALF + d0 + i]), p.weight_offset)));
+    float c, s;
+    const int64_t co = pos * p.cos_row + d0 + i;
+    if (p.cos_float) {
+      c = static_cast<const float*>(p.cos_sin)[co];
+      s = static_cast<const float*>(p.cos_sin)[co + HALF];
+    } else {
+      c = __bfloat162float(static_cast<const __nv_bfloat16*>(p.cos_sin)[co]);
+      s = __bfloat162float(static_cast<const __nv_bfloat16*>(p.cos_sin)[co + HALF]);
+    }
+    x[i] = bf16r(__fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s)));
+    y[i] = bf16r(__fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s)));
+  }
+  if (!is_k) {
+    __nv_bfloat16* q = static_cast<__nv_bfloat16*>(p.q) + row * p.q_row + (int64_t)local * D;
+#pragma unroll
+    for (int i = 0; i < E2; ++i) {
+      q[d0 + i] = __float2bfloat16_rn(x[i]);
+      q[HALF + d0 + i] = __float2bfloat16_rn(y[i]);
+    }
+    if (p.gate) {
+      __nv_bfloat16* g = static_cast<__nv_bfloat16*>(p.gate) + row * p.gate_row + (int64_t)local * D;
+#pragma unroll
+      for (int i = 0; i < E2; ++i) {
+        g[d0 + i] = qkv[base + D + d0 + i];
+        g[HALF + d0 + i] = qkv[base + D + HALF + d0 + i];
+      }
+    }
+    return;
+  }
+  if (row >= p.slot_rows) return;
+  const int64_t slot = p.slot_long ? static_cast<const int64_t*>(p.slots)[row]
+                                   : static_cast<const int32_t*>(p.slots)[row];
+  if (slot < 0) return;  // padding token: nothing to append
+  if (slot >= (int64_t)p.pages * p.page_size) {
+    if (lane == 0) report(p.status, kStatusBadSlot);
+    return;
+  }
+  const float kg = *p.k_global, vg = *p.v_global;
+  if (!(isfinite(kg) && kg > 0.0f && isfinite(vg) && vg > 0.0f)) {
+    if (lane == 0) report(p.status, kStatusBadKvScale);
+    return;
+  }
+  const int64_t page = slot / p.page_size, entry = slot % p.page_size;
+  const int64_t data = page * p.data_page + entry * p.data_row + (int64_t)local * p.data_head;
+  const int64_t sfo = page * p.sf_page + entry * p.sf_row + (int64_t)local * p.sf_head;
+  const int64_t vbase = row * p.input_row + (int64_t)p.qheads * 2 * D + (int64_t)p.kvheads * D + (int64_t)local * D;
+#pragma unroll
+  for (int which = 0; which < 2; ++which) {
+    uint8_t* codes = static_cast<uint8_t*>(which ? p.v_cache : p.k_cache) + data;
+    uint8_t* scales = static_cast<uint8_t*>(which ? p.v_scales : p.k_scales) + sfo;
+    const float g = which ? vg : kg;
+    if (which) {
+#pragma unroll
+      for (int i = 0; i < E2; ++i) {
+        x[i] = __bfloat162float(qkv[vbase + d0 + i]);
+        y[i] = __bfloat162float(qkv[vbase + HALF + d0 + i]);
+      }
+    }
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const float* v = half ? y : x;
+      const int dstart = half * HALF + d0;
+      float amax = 0.0f;
+#pragma unroll
+      for (int i = 0; i < E2; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+      for (int d = 1; d < 16 / E2; d <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
+      const uint32_t code = f_to_e4m3(__fdiv_rn(amax, __fmul_rn(6.0f, g)));
+      const float scale = e4m3_to_f(code);
+      const float inverse = scale > 0.0f ? __fdiv_rn(1.0f, __fmul_rn(scale, g)) : 0.0f;
+      if ((dstart & 15) == 0) scales[dstart >> 4] = (uint8_t)code;
+      if constexpr (E2 == 1) {
+        const float mine = __fmul_rn(v[0], inverse);
+        const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
+        if ((lane & 1) == 0) codes[dstart >> 1] = (uint8_t)f2_to_e2m1x2(mine, other);
+      } else {
+#pragma unroll
+        for (int i = 0; i < E2; i += 2)
+          codes[(dstart + i) >> 1] = (uint8_t)f2_to_e2m1x2(__fmul_rn(v[i], inverse), __fmul_rn(v[i + 1], inverse));
+      }
+    }
+  }
+}
+
+// One CTA per row, thread t owns 16 consecutive columns.
+__global__ void gate_fp8_kernel(const __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ gate,
+                                int64_t out_row, int64_t gate_row, uint8_t* __restrict__ fp8, int64_t fp8_row,
+                                float* __restrict__ scale_out, int cols) {
+  __shared__ float scratch[33];
+  const int64_t row = blockIdx.x;
+  const int t = threadIdx.x;
+  const bool active = 16 * t < cols;
+  float v[16];
+  float amax = 0.0f;
+  if (active) {
+    float o[16], g[16];
+    load16_bf16(out + row * out_row + 16 * t, o);
+    load16_bf16(gate + row * gate_row + 16 * t, g);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      v[j] = bf16r(__fmul_rn(o[j], bf16r(sigmoid_f(g[j]))));
+      amax = fmaxf(amax, fabsf(v[j]));
+    }
+  }
+  amax = block_max(amax, scratch);
+  const float scale = fmaxf(__fdiv_rn(amax, 448.0f), 1.17549435e-38f);
+  if (t == 0) scale_out[row] = scale;
+  if (!active) return;
+  uint32_t w[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    w[k] = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) w[k] |= f_to_e4m3(__fdiv_rn(v[4 * k + j], scale)) << (8 * j);
+  }
+  reinterpret_cast<uint4*>(fp8 + row * fp8_row)[t] = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Weight quantiser: fp32 [rows, K] -> NVFP4 (same arithmetic as the producer).
+__global__ void nvfp4_quant_kernel(const float* __restrict__ w, int64_t rows, int k, const float* __restrict__ g,
+                                   uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
+  const int64_t groups = k >> 4;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= rows * groups) return;
+  const int64_t row = idx / groups, grp = idx % groups;
+  float v[16];
+  const float4* src = reinterpret_cast<const float4*>(w + row * k + grp * 16);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 f = src[i];
+    v[4 * i] = f.x;
+    v[4 * i + 1] = f.y;
+    v[4 * i + 2] = f.z;
+    v[4 * i + 3] = f.w;
+  }
+  uint2 packed;
+  const uint32_t code = nvfp4_quant16(v, *g, packed);
+  reinterpret_cast<uint2*>(q + row * (k >> 1))[grp] = packed;
+  sf[sf_offset(row, grp, (groups + 3) & ~3)] = (uint8_t)code;
+}
+
+// Weight quantiser: fp32 [rows, K] -> E4M3 with scale[row] = max(amax/448, FLT_MIN).
+__global__ void fp8_rows_kernel(const float* __restrict__ w, int k, uint8_t* __restrict__ q,
+                                float* __restrict__ scale_out) {
+  __shared__ float scratch[33];
+  const int64_t row = blockIdx.x;
+  float amax = 0.0f;
+  for (int c = threadIdx.x; c < k; c += blockDim.x) amax = fmaxf(amax, fabsf(w[row * k + c]));
+  amax = block_max(amax, scratch);
+  const float scale = fmaxf(__fdiv_rn(amax, 448.0f), 1.17549435e-38f);
+  if (threadIdx.x == 0) scale_out[row] = scale;
+  for (int c = threadIdx.x; c < k; c += blockDim.x) q[row * k + c] = (uint8_t)f_to_e4m3(__fdiv_rn(w[row * k + c], scale));
+}
+
+// Paged NVFP4 KV -> bf16 K [Hkv][tokens][D] and V^T [Hkv][D][v_stride].  The
+// stored values are e2m1 * e4m3 (exact in bf16); the fp32 global multiplier
+// is applied by the attention kernel.  One CTA per (64-token tile, head).
+template <int D>
+__global__ void __launch_bounds__(256) kv_dequant_kernel(const uint8_t* __restrict__ kc, const uint8_t* __restrict__ vc,
+                                                         const uint8_t* __restrict__ ksf, const uint8_t* __restrict__ vsf,
+                                                         const int32_t* __restrict__ block_table, int tokens, int page_size,
+                                                         int64_t data_page, int64_t data_row, int64_t data_head,
+                                                         int64_t sf_page, int64_t sf_row, int64_t sf_head,
+                                                         __nv_bfloat16* __restrict__ k_out, __nv_bfloat16* __restrict__ vt_out,
+                                                         int64_t k_head_stride, int64_t vt_head_stride, int64_t vt_row) {
+  __shared__ __nv_bfloat16 vtile[64][D + 8];
+  const int head = blockIdx.y;
+  const int t0 = blockIdx.x * 64;
+  const float lut[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+  // Each thread dequantises 8 consecutive values (4 code bytes) of one token.
+  constexpr int PER_TOKEN = D / 8;
+  for (int i = threadIdx.x; i < 64 * PER_TOKEN; i += blockDim.x) {
+    const int tl = i / PER_TOKEN, chunk = i % PER_TOKEN;
+    const int tok = t0 + tl;
+    float kv8[2][8];
+    if (tok < tokens) {
+      const int64_t page = block_table[tok / page_size], entry = tok % page_size;
+      const int64_t dbase = page * data_page + entry * data_row + (int64_t)head * data_head + chunk * 4;
+      const int64_t sbase = page * sf_page + entry * sf_row + (int64_t)head * sf_head + (chunk * 8) / 16;
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        const uint32_t bytes = *reinterpret_cast<const uint32_t*>((which ? vc : kc) + dbase);
+        const float s = e4m3_to_f((which ? vsf : ksf)[sbase]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t c = (bytes >> (4 * j)) & 0xF;
+          const float m = lut[c & 7];
+          kv8[which][j] = __fmul_rn((c & 8) ? -m : m, s);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) kv8[0][j] = kv8[1][j] = 0.0f;
+    }
+    if (tok < tokens) {
+      uint4 packed;
+      __nv_bfloat162* pk = reinterpret_cast<__nv_bfloat162*>(&packed);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) pk[j] = __floats2bfloat162_rn(kv8[0][2 * j], kv8[0][2 * j + 1]);
+      *reinterpret_cast<uint4*>(k_out + head * k_head_stride + (int64_t)tok * D + chunk * 8) = packed;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) vtile[tl][chunk * 8 + j] = __float2bfloat16_rn(kv8[1][j]);
+  }
+  __syncthreads();
+  // Write V^T rows: for each d, 64 consecutive tokens (128 bytes).
+  const int valid = min(64, (int)((vt_row - t0)));
+  for (int i = threadIdx.x; i < D * 32; i += blockDim.x) {
+    const int d = i / 32, pair = i % 32;
+    if (2 * pair < valid) {
+      __nv_bfloat162 v2;
+      v2.x = vtile[2 * pair][d];
+      v2.y = vtile[2 * pair + 1][d];
+      *reinterpret_cast<__nv_bfloat162*>(vt_out + head * vt_head_stride + (int64_t)d * vt_row + t0 + 2 * pair) = v2;
+    }
+  }
+}
+
+// Element-wise conversion check: E2M1 codes of in[i] (pairs packed as the
+// kernels pack them), E4M3 codes, and fexp / sigmoid of in[i].
+__global__ void convert_probe_kernel(const float* __restrict__ in, uint8_t* __restrict__ e2m1_pairs,
+                                     uint8_t* __restrict__ e4m3, float* __restrict__ ex, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float v = in[i];
+  e4m3[i] = (uint8_t)f_to_e4m3(v);
+  ex[2 * i] = fexp(v);
+  ex[2 * i + 1] = sigmoid_f(v);
+  if ((i & 1) == 0 && i + 1 < n) e2m1_pairs[i >> 1] = (uint8_t)f2_to_e2m1x2(v, in[i + 1]);
+  if ((i & 7) == 0 && i + 7 < n) {
+    float v8[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v8[j] = in[i + j];
+    reinterpret_cast<uint32_t*>(e2m1_pairs + (n >> 1))[i >> 3] = f8_to_e2m1x8(v8);
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+int qi_norm_pack(const void* x, const void* residual, const void* gamma, const float* global_scale, void* q,
+                 void* scales, void* updated, int rows, int hidden, float eps, float weight_offset,
+                 cudaStream_t stream) {
+  if (rows < 1 || hidden < 64 || hidden % 64 || hidden > 16384 || !x || !gamma || !global_scale || !q || !scales)
+    return (int)cudaErrorInvalidValue;
+  if (!aligned16(x) || (residual && !aligned16(residual)) || (updated && !aligned16(updated)) || !aligned16(gamma) ||
+      (reinterpret_cast<uintptr_t>(q) & 7))
+    return (int)cudaErrorInvalidValue;
+  const int threads = ((hidden / 16) + 31) / 32 * 32;
+  norm_kernel<true><<<rows, threads, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(residual),
+      static_cast<const __nv_bfloat16*>(gamma), global_scale, static_cast<uint8_t*>(q), static_cast<uint8_t*>(scales),
+      static_cast<__nv_bfloat16*>(updated), nullptr, hidden, eps, weight_offset);
+  return (int)cudaPeekAtLastError();
+}
+
+int qi_rms_norm(const void* x, const void* residual, const void* gamma, void* out, void* updated, int rows,
+                int hidden, float eps, float weight_offset, cudaStream_t stream) {
+  if (rows < 1 || hidden < 64 || hidden % 64 || hidden > 16384 || !x || !gamma || !out)
+    return (int)cudaErrorInvalidValue;
+  if (!aligned16(x) || (residual && !aligned16(residual)) || !aligned16(out) || !aligned16(gamma) ||
+      (updated && !aligned16(updated)))
+    return (int)cudaErrorInvalidValue;
+  const int threads = ((hidden / 16) + 31) / 32 * 32;
+  norm_kernel<false><<<rows, threads, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(residual),
+      static_cast<const __nv_bfloat16*>(gamma), nullptr, nullptr, nullptr, static_cast<__nv_bfloat16*>(updated),
+      static_cast<__nv_bfloat16*>(out), hidden, eps, weight_offset);
+  return (int)cudaPeekAtLastError();
+}
+
+int nvfp4_norm_pack_launch(const void* x, const void* r, const void* w, const void* global, void* q, void* scale,
+                           void* updated, int rows, cudaStream_t stream) {
+  if (rows < 1 || rows > 8192 || !x || !r || !w || !global || !q || !scale || !updated)
+    return (int)cudaErrorInvalidValue;
+  return qi_norm_pack(x, r, w, static_cast<const float*>(global), q, scale, updated, rows, 5120, 1e-6f, 1.0f, stream);
+}
+
+int nvfp4_norm_pack_metadata(int* out) {
+  if (!out) return (int)cudaErrorInvalidValue;
+  cudaFuncAttributes attr{};
+  const cudaError_t status = cudaFuncGetAttributes(&attr, norm_kernel<true>);
+  if (status != cudaSuccess) return (int)status;
+  out[0] = attr.numRegs;
+  out[1] = (int)attr.sharedSizeBytes;
+  out[2] = (int)attr.localSizeBytes;
+  return 0;
+}
+
+int qi_qk_rope_kv_append(const QiFront* p, cudaStream_t stream) {
+  if (!p || p->rows < 1 || p->qheads < 1 || p->kvheads < 1 || !p->qkv || !p->q_weight || !p->k_weight ||
+      !p->cos_sin || !p->positions || !p->q || p->page_size < 1 || p->pages < 0)
+    return (int)cudaErrorInvalidValue;
+  if (p->qheads % p->kvheads) return (int)cudaErrorInvalidValue;
+  if (p->slot_rows > 0 && (!p->slots || !p->k_global || !p->v_global || !p->k_cache || !p->v_cache ||
+                           !p->k_scales || !p->v_scales))
+    return (int)cudaErrorInvalidValue;
+  if (p->slot_rows > p->rows) return (int)cudaErrorInvalidValue;
+  const dim3 grid(p->rows, (p->qheads + p->kvheads + 7) / 8);
+  switch (p->head_dim) {
+    case 64: front_kernel<1><<<grid, 256, 0, stream>>>(*p); break;
+    case 128: front_kernel<2><<<grid, 256, 0, stream>>>(*p); break;
+    case 256: front_kernel<4><<<grid, 256, 0, stream>>>(*p); break;
+    default: return (int)cudaErrorInvalidValue;
+  }
+  return (int)cudaPeekAtLastError();
+}
+
+int qi_qk_rope_kv_append_resources(int* out) {
+  if (!out) return (int)cudaErrorInvalidValue;
+  cudaFuncAttributes a{};
+  int occupancy = 0;
+  cudaError_t e = cudaFuncGetAttributes(&a, front_kernel<2>);
+  if (e != cudaSuccess) return (int)e;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occupancy, front_kernel<2>, 256, 0);
+  if (e != cudaSuccess) return (int)e;
+  out[0] = (int)sizeof(QiFront);
+  out[1] = a.numRegs;
+  out[2] = (int)a.sharedSizeBytes;
+  out[3] = (int)a.localSizeBytes;
+  out[4] = occupancy;
+  return 0;
+}
+
+int nvfp4_attention_front(RefFront f, cudaStream_t stream) {
+  // The reference's D256 ABI: no MRoPE, rotary covering the whole head.
+  if (f.rows < 1 || f.qheads < 1 || f.kvheads < 1 || f.rotary != 256 || f.mrope_h || f.mrope_w)
+    return (int)cudaErrorInvalidValue;
+  QiFront p{};
+  p.qkv = f.qkv;
+  p.q_weight = f.qw;
+  p.k_weight = f.kw;
+  p.cos_sin = f.cos_sin;
+  p.positions = f.positions;
+  p.slots = f.slots;
+  p.k_global = f.k_scale;
+  p.v_global = f.v_scale;
+  p.k_cache = f.k;
+  p.v_cache = f.v;
+  p.k_scales = f.ks;
+  p.v_scales = f.vs;
+  p.q = f.q;
+  p.gate = f.gate;
+  p.status = nullptr;
+  p.rows = f.rows;
+  p.qheads = f.qheads;
+  p.kvheads = f.kvheads;
+  p.head_dim = 256;
+  p.slot_rows = f.slot_rows;
+  p.pages = f.pages;
+  p.page_size = f.page_size;
+  p.cos_float = f.cos_float;
+  p.pos_long = f.pos_long;
+  p.slot_long = f.slot_long;
+  p.input_row = f.input_row;
+  p.cos_row = f.cos_row;
+  p.q_row = (int64_t)f.qheads * 256;
+  p.gate_row = (int64_t)f.qheads * 256;
+  p.data_page = f.data_page;
+  p.data_row = f.data_row;
+  p.data_head = f.data_head;
+  p.sf_page = f.sf_page;
+  p.sf_row = f.sf_row;
+  p.sf_head = f.sf_head;
+  p.eps = f.epsilon;
+  p.weight_offset = 1.0f;
+  if (f.pos_t != 1) return (int)cudaErrorInvalidValue;
+  return qi_qk_rope_kv_append(&p, stream);
+}
+
+int nvfp4_attention_front_resources(int* out) {
+  if (!out) return (int)cudaErrorInvalidValue;
+  const int rc = qi_qk_rope_kv_append_resources(out);
+  if (rc) return rc;
+  out[0] = (int)sizeof(RefFront);
+  return 0;
+}
+
+int qi_gate_fp8(const void* out, const void* gate, int64_t out_row, int64_t gate_row, void* fp8, int64_t fp8_row,
+                float* scale, int rows, int cols, cudaStream_t stream) {
+  if (rows < 1 || cols < 16 || cols % 16 || cols > 16384 || !out || !gate || !fp8 || !scale)
+    return (int)cudaErrorInvalidValue;
+  if (!aligned16(out) || !aligned16(gate) || !aligned16(fp8) || out_row % 8 || gate_row % 8 || fp8_row % 16)
+    return (int)cudaErrorInvalidValue;
+  const int threads = ((cols / 16) + 31) / 32 * 32;
+  gate_fp8_kernel<<<rows, threads, 0, stream>>>(static_cast<const __nv_bfloat16*>(out),
+                                                static_cast<const __nv_bfloat16*>(gate), out_row, gate_row,
+                                                static_cast<uint8_t*>(fp8), fp8_row, scale, cols);
+  return (int)cudaPeekAtLastError();
+}
+
+int qi_nvfp4_quantize(const float* w, int64_t rows, int k, const float* global_scale, void* q, void* scales,
+                      cudaStream_t stream) {
+  if (rows < 1 || k < 64 || k % 64 || !w || !global_scale || !q || !scales || !aligned16(w))
+    return (int)cudaErrorInvalidValue;
+  const int64_t work = rows * (k / 16);
+  const int threads = 256;
+  const int64_t blocks = (work + threads - 1) / threads;
+  if (blocks > 0x7fffffff) return (int)cudaErrorInvalidValue;
+  nvfp4_quant_kernel<<<(unsigned)blocks, threads, 0, stream>>>(w, rows, k, global_scale, static_cast<uint8_t*>(q),
+                                                               static_cast<uint8_t*>(scales));
+  return (int)cudaPeekAtLastError();
+}
+
+int qi_fp8_quantize_rows(const float* w, int rows, int k, void* q, float* scales, cudaStream_t stream) {
+  if (rows < 1 || k < 1 || !w || !q || !scales) return (int)cudaErrorInvalidValue;
+  fp8_rows_kernel<<<rows, 256, 0, stream>>>(w, k, static_cast<uint8_t*>(q), scales);
+  return (int)cudaPeekAtLastError();
+}
+
+int qi_kv_dequant(const QiKvView* kv, const int32_t* block_table, int tokens, void* k_out, void* vt_out,
+                  int64_t vt_row, cudaStream_t stream) {
+  if (!kv || !block_table || tokens < 1 || !k_out || !vt_out || vt_row < tokens || vt_row % 64)
+    return (int)cudaErrorInvalidValue;
+  if (!kv->k_cache || !kv->v_cache || !kv->k_scales || !kv->v_scales || kv->kvheads < 1 || kv->page_size < 1)
+    return (int)cudaErrorInvalidValue;
+  const dim3 grid((tokens + 63) / 64, kv->kvheads);
+  const int64_t ks = (int64_t)tokens * kv->head_dim, vs = (int64_t)kv->head_dim * vt_row;
+#define QI_KVD(DD)                                                                                                  \
+  kv_dequant_kernel<DD><<<grid, 256, 0, stream>>>(                                                                  \
+      static_cast<const uint8_t*>(kv->k_cache), static_cast<const uint8_t*>(kv->v_cache),                          \
+      static_cast<const uint8_t*>(kv->k_scales), static_cast<const uint8_t*>(kv->v_scales), block_table, tokens,   \
+      kv->page_size, kv->data_page, kv->data_row, kv->data_head, kv->sf_page, kv->sf_row, kv->sf_head,            \
+      static_cast<__nv_bfloat16*>(k_out), static_cast<__nv_bfloat16*>(vt_out), ks, vs, vt_row)
+  switch (kv->head_dim) {
+    case 64: QI_KVD(64); break;
+    case 128: QI_KVD(128); break;
+    default: return (int)cudaErrorInvalidValue;
+  }
+#undef QI_KVD
+  return (int)cudaPeekAtLastError();
+}
+
+int qi_convert_probe(const float* in, void* e2m1_pairs, void* e4m3, float* ex, int n, cudaStream_t stream) {
+  if (!in || !e2m1_pairs || !e4m3 || !ex || n < 8 || n % 8) return (int)cudaErrorInvalidValue;
+  convert_probe_kernel<<<(n + 255) / 256, 256, 0, stream>>>(in, static_cast<uint8_t*>(e2m1_pairs),
+                                                             static_cast<uint8_t*>(e4m3), ex, n);
+  return (int)cudaPeekAtLastError();
+}
+
+int qi_abi_struct_sizes(int* out) {
+  if (!out) return (int)cudaErrorInvalidValue;
+  out[0] = (int)sizeof(RefFront);
+  out[1] = (int)sizeof(QiFront);
+  out[2] = (int)sizeof(QiGemm);
+  out[3] = (int)sizeof(QiKvView);
+  out[4] = (int)sizeof(QiAttention);
+  return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,271 @@
+"""Torch-facing operators over the C ABI (one function per kernel entry point).
+
+Mirrors the reference's operator wrappers (``kernels/nvfp4_norm_pack.py:115-159``,
+``kernels/nvfp4_attention_front.py:145-237``): arguments are validated on the
+host (``ValueError``), outputs are allocated by the caller side in torch, the
+launch goes to the current torch stream, and a non-zero launch status raises
+``RuntimeError``.  There is no CPU path: every call enters the CUDA library.
+"""
+
+import ctypes as ct
+import math
+
+import torch
+
+from . import _native as N
+
+
+def _ptr(t):
+    return None if t is None else ct.c_void_p(t.data_ptr())
+
+
+def _stream(dev):
+    return ct.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("the prefill kernels take CUDA tensors only")
+
+
+def scale_groups_padded(k):
+    return ((k // 16) + 3) // 4 * 4
+
+
+def scale_buffer_bytes(rows, k):
+    return (rows + 127) // 128 * 128 * scale_groups_padded(k)
+
+
+def norm_pack(x, residual, gamma, global_scale, *, eps=1e-6, weight_offset=1.0, q=None, scales=None,
+              updated=None, want_updated=True):
+    """Residual add + RMSNorm -> NVFP4 (e2m1 codes + swizzled e4m3 scales) and
+    the bf16 updated residual.  ``residual=None`` is the first layer."""
+    _cuda(x, residual, gamma, global_scale)
+    rows, h = x.shape
+    if x.dtype != torch.bfloat16 or gamma.dtype != torch.bfloat16 or tuple(gamma.shape) != (h,):
+        raise ValueError("norm_pack expects bf16 [rows, H] input and bf16 [H] gamma")
+    if residual is not None and (residual.shape != x.shape or residual.dtype != x.dtype):
+        raise ValueError("residual must match x")
+    if global_scale.dtype != torch.float32 or global_scale.numel() != 1:
+        raise ValueError("global scale must be one fp32 device scalar")
+    if q is None:
+        q = torch.empty((rows, h // 2), dtype=torch.uint8, device=x.device)
+    if scales is None:
+        scales = torch.empty(scale_buffer_bytes(rows, h), dtype=torch.uint8, device=x.device)
+    if updated is None and want_updated:
+        updated = torch.empty_like(x)
+    N.check(N.lib().qi_norm_pack(_ptr(x), _ptr(residual), _ptr(gamma), _ptr(global_scale), _ptr(q), _ptr(scales),
+                                 _ptr(updated), rows, h, eps, weight_offset, _stream(x.device)), "qi_norm_pack")
+    return q, scales, updated
+
+
+def rms_norm(x, residual, gamma, *, eps=1e-6, weight_offset=1.0, out=None, updated=None):
+    _cuda(x, residual, gamma)
+    rows, h = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    N.check(N.lib().qi_rms_norm(_ptr(x), _ptr(residual), _ptr(gamma), _ptr(out), _ptr(updated), rows, h, eps,
+                                weight_offset, _stream(x.device)), "qi_rms_norm")
+    return out
+
+
+class PagedKV:
+    """NVFP4 paged KV of one layer: codes [pages, page_size, Hkv, D/2] u8 and
+    E4M3 scales [pages, page_size, Hkv, D/16] u8, for K and for V."""
+
+    def __init__(self, pages, page_size, kvheads, head_dim, device):
+        self.page_size, self.kvheads, self.head_dim = page_size, kvheads, head_dim
+        shape = (pages, page_size, kvheads, head_dim // 2)
+        sshape = (pages, page_size, kvheads, head_dim // 16)
+        self.k = torch.zeros(shape, dtype=torch.uint8, device=device)
+        self.v = torch.zeros(shape, dtype=torch.uint8, device=device)
+        self.ks = torch.zeros(sshape, dtype=torch.uint8, device=device)
+        self.vs = torch.zeros(sshape, dtype=torch.uint8, device=device)
+
+    @property
+    def pages(self):
+        return self.k.shape[0]
+
+    def view(self):
+        v = N.QiKvView()
+        v.k_cache, v.v_cache = self.k.data_ptr(), self.v.data_ptr()
+        v.k_scales, v.v_scales = self.ks.data_ptr(), self.vs.data_ptr()
+        v.kvheads, v.head_dim, v.page_size = self.kvheads, self.head_dim, self.page_size
+        v.data_page, v.data_row, v.data_head = self.k.stride(0), self.k.stride(1), self.k.stride(2)
+        v.sf_page, v.sf_row, v.sf_head = self.ks.stride(0), self.ks.stride(1), self.ks.stride(2)
+        return v
+
+
+def qk_rope_kv_append(qkv, positions, q_weight, k_weight, cos_sin, slots, kv, k_global, v_global, *, qheads,
+                      kvheads, head_dim, eps=1e-6, weight_offset=1.0, q=None, gate=None, want_gate=True,
+                      status=None):
+    """QK-norm + RoPE (rotary == head_dim) + gate split + NVFP4 paged KV append."""
+    _cuda(qkv, positions, q_weight, k_weight, cos_sin, slots, k_global, v_global)
+    rows = qkv.shape[0]
+    d = head_dim
+    if qkv.dtype != torch.bfloat16 or qkv.stride(-1) != 1 or qkv.shape[1] != (2 * qheads + 2 * kvheads) * d:
+        raise ValueError("qkv must be bf16 [rows, (2Hq + 2Hkv) D]")
+    if cos_sin.dtype not in (torch.float32, torch.bfloat16) or cos_sin.shape[1] != d:
+        raise ValueError("cos_sin must be [maxpos, D] fp32 or bf16")
+    if positions.dtype not in (torch.int32, torch.int64) or slots.dtype not in (torch.int32, torch.int64):
+        raise ValueError("positions and slots are int32 or int64")
+    if q is None:
+        q = torch.empty((rows, qheads * d), dtype=torch.bfloat16, device=qkv.device)
+    if gate is None and want_gate:
+        gate = torch.empty((rows, qheads * d), dtype=torch.bfloat16, device=qkv.device)
+    p = N.QiFront()
+    p.qkv, p.q_weight, p.k_weight, p.cos_sin = qkv.data_ptr(), q_weight.data_ptr(), k_weight.data_ptr(), cos_sin.data_ptr()
+    p.positions, p.slots = positions.data_ptr(), slots.data_ptr()
+    p.k_global, p.v_global = k_global.data_ptr(), v_global.data_ptr()
+    p.k_cache, p.v_cache, p.k_scales, p.v_scales = kv.k.data_ptr(), kv.v.data_ptr(), kv.ks.data_ptr(), kv.vs.data_ptr()
+    p.q = q.data_ptr()
+    p.gate = gate.data_ptr() if gate is not None else None
+    p.status = status.data_ptr() if status is not None else None
+    p.rows, p.qheads, p.kvheads, p.head_dim = rows, qheads, kvheads, d
+    p.slot_rows, p.pages, p.page_size = slots.numel(), kv.pages, kv.page_size
+    p.cos_float = int(cos_sin.dtype == torch.float32)
+    p.pos_long, p.slot_long = int(positions.dtype == torch.int64), int(slots.dtype == torch.int64)
+    p.input_row, p.cos_row = qkv.stride(0), cos_sin.stride(0)
+    p.q_row = q.stride(0)
+    p.gate_row = gate.stride(0) if gate is not None else 0
+    p.data_page, p.data_row, p.data_head = kv.k.stride(0), kv.k.stride(1), kv.k.stride(2)
+    p.sf_page, p.sf_row, p.sf_head = kv.ks.stride(0), kv.ks.stride(1), kv.ks.stride(2)
+    p.eps, p.weight_offset = eps, weight_offset
+    N.check(N.lib().qi_qk_rope_kv_append(ct.byref(p), _stream(qkv.device)), "qi_qk_rope_kv_append")
+    return q, gate
+
+
+def gate_fp8(out, gate, *, fp8=None, scale=None):
+    """bf16(out * bf16(sigmoid(gate))) -> E4M3 with a per-row fp32 scale."""
+    _cuda(out, gate)
+    rows, cols = out.shape
+    if fp8 is None:
+        fp8 = torch.empty((rows, cols), dtype=torch.uint8, device=out.device)
+    if scale is None:
+        scale = torch.empty(rows, dtype=torch.float32, device=out.device)
+    N.check(N.lib().qi_gate_fp8(_ptr(out), _ptr(gate), out.stride(0), gate.stride(0), _ptr(fp8), fp8.stride(0),
+                                _ptr(scale), rows, cols, _stream(out.device)), "qi_gate_fp8")
+    return fp8, scale
+
+
+def _gemm_struct(kind, epilogue, m, n, k, a, b, sfa=None, sfb=None, alpha=None, alpha_value=1.0):
+    g = N.QiGemm()
+    g.kind, g.epilogue, g.m, g.n, g.k = kind, epilogue, m, n, k
+    g.a, g.b = a.data_ptr(), b.data_ptr()
+    g.sfa = sfa.data_ptr() if sfa is not None else None
+    g.sfb = sfb.data_ptr() if sfb is not None else None
+    g.alpha = alpha.data_ptr() if alpha is not None else None
+    g.alpha_value = alpha_value
+    return g
+
+
+def gemm_nvfp4(a, sfa, b, sfb, *, m, n, k, alpha=None, alpha_value=1.0, out=None, out_dtype=torch.bfloat16):
+    """A [m, k/2] NVFP4 . B [n, k/2]^T with block scales -> bf16 (or fp32) [m, n]."""
+    _cuda(a, sfa, b, sfb, alpha)
+    epi = N.EPI_BF16 if out_dtype == torch.bfloat16 else N.EPI_F32
+    if out is None:
+        out = torch.empty((m, n), dtype=out_dtype, device=a.device)
+    g = _gemm_struct(N.GEMM_NVFP4, epi, m, n, k, a, b, sfa, sfb, alpha, alpha_value)
+    g.out, g.ldo = out.data_ptr(), out.stride(0)
+    N.check(N.lib().qi_gemm(ct.byref(g), _stream(a.device)), "qi_gemm")
+    return out
+
+
+def gemm_swiglu_nvfp4(a, sfa, b, sfb, act_global, *, m, n, k, alpha=None, alpha_value=1.0, act_q=None,
+                      act_sf=None):
+    """gate_up GEMM with the SiLU-and-mul + NVFP4 epilogue: output [m, n/4]
+    codes (n/2 channels) and the swizzled scales of K = n/2."""
+    _cuda(a, sfa, b, sfb, alpha, act_global)
+    inter = n // 2
+    if act_q is None:
+        act_q = torch.empty((m, inter // 2), dtype=torch.uint8, device=a.device)
+    if act_sf is None:
+        act_sf = torch.empty(scale_buffer_bytes(m, inter), dtype=torch.uint8, device=a.device)
+    g = _gemm_struct(N.GEMM_NVFP4, N.EPI_SWIGLU_NVFP4, m, n, k, a, b, sfa, sfb, alpha, alpha_value)
+    g.act_q, g.act_sf, g.act_global, g.act_ld = act_q.data_ptr(), act_sf.data_ptr(), act_global.data_ptr(), act_q.stride(0)
+    N.check(N.lib().qi_gemm(ct.byref(g), _stream(a.device)), "qi_gemm")
+    return act_q, act_sf
+
+
+def gemm_e4m3(a, b, *, m, n, k, row_scale=None, col_scale=None, alpha_value=1.0, out=None,
+              out_dtype=torch.bfloat16):
+    """A [m, k] E4M3 . B [n, k]^T -> bf16 scaled by row_scale[m] * col_scale[n]
+    (or fp32 times alpha_value when out_dtype is float32)."""
+    _cuda(a, b, row_scale, col_scale)
+    if out is None:
+        out = torch.empty((m, n), dtype=out_dtype, device=a.device)
+    if out_dtype == torch.float32:
+        epi = N.EPI_F32
+    else:
+        epi = N.EPI_BF16_ROWCOL if row_scale is not None else N.EPI_BF16
+    g = _gemm_struct(N.GEMM_E4M3, epi, m, n, k, a, b, alpha_value=alpha_value)
+    g.row_scale = row_scale.data_ptr() if row_scale is not None else None
+    g.col_scale = col_scale.data_ptr() if col_scale is not None else None
+    g.out, g.ldo = out.data_ptr(), out.stride(0)
+    N.check(N.lib().qi_gemm(ct.byref(g), _stream(a.device)), "qi_gemm")
+    return out
+
+
+def kv_dequant(kv, block_table, tokens, *, k_out=None, vt_out=None):
+    """Paged NVFP4 KV of one request -> bf16 K [Hkv, tokens, D] and V^T
+    [Hkv, D, vt_row] (vt_row = tokens rounded up to 64)."""
+    _cuda(block_table)
+    vt_row = (tokens + 63) // 64 * 64
+    d = kv.head_dim
+    if k_out is None:
+        k_out = torch.empty((kv.kvheads, tokens, d), dtype=torch.bfloat16, device=kv.k.device)
+    if vt_out is None:
+        vt_out = torch.empty((kv.kvheads, d, vt_row), dtype=torch.bfloat16, device=kv.k.device)
+    view = kv.view()
+    N.check(N.lib().qi_kv_dequant(ct.byref(view), _ptr(block_table), tokens, _ptr(k_out), _ptr(vt_out), vt_row,
+                                  _stream(kv.k.device)), "qi_kv_dequant")
+    return k_out, vt_out
+
+
+def prefill_attention(q, k, vt, *, history, qheads, kvheads, head_dim, k_global, v_global, out=None,
+                      softmax_scale=None, status=None, kv_tokens=None):
+    """Causal GQA attention of ``rows`` queries at positions history.. over
+    keys 0 .. history+rows-1 held as bf16 K / V^T (from :func:`kv_dequant`)."""
+    _cuda(q, k, vt, k_global, v_global)
+    rows = q.shape[0]
+    if out is None:
+        out = torch.empty((rows, qheads * head_dim), dtype=torch.bfloat16, device=q.device)
+    p = N.QiAttention()
+    p.q, p.k, p.vt, p.out = q.data_ptr(), k.data_ptr(), vt.data_ptr(), out.data_ptr()
+    p.k_global, p.v_global = k_global.data_ptr(), v_global.data_ptr()
+    p.status = status.data_ptr() if status is not None else None
+    p.rows, p.history = rows, history
+    p.kv_tokens = kv_tokens if kv_tokens is not None else k.shape[1]
+    p.qheads, p.kvheads, p.head_dim = qheads, kvheads, head_dim
+    p.q_row, p.out_row, p.vt_row = q.stride(0), out.stride(0), vt.shape[2]
+    p.softmax_scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(head_dim)
+    N.check(N.lib().qi_prefill_attention(ct.byref(p), _stream(q.device)), "qi_prefill_attention")
+    return out
+
+
+def nvfp4_quantize(w, global_scale, *, q=None, scales=None):
+    """fp32 [rows, K] -> NVFP4 codes [rows, K/2] + swizzled scales."""
+    _cuda(w, global_scale)
+    rows, k = w.shape
+    if w.dtype != torch.float32 or not w.is_contiguous():
+        raise ValueError("weights must be contiguous fp32")
+    if q is None:
+        q = torch.empty((rows, k // 2), dtype=torch.uint8, device=w.device)
+    if scales is None:
+        scales = torch.zeros(scale_buffer_bytes(rows, k), dtype=torch.uint8, device=w.device)
+    N.check(N.lib().qi_nvfp4_quantize(_ptr(w), rows, k, _ptr(global_scale), _ptr(q), _ptr(scales),
+                                      _stream(w.device)), "qi_nvfp4_quantize")
+    return q, scales
+
+
+def fp8_quantize_rows(w, *, q=None, scales=None):
+    _cuda(w)
+    rows, k = w.shape
+    if q is None:
+        q = torch.empty((rows, k), dtype=torch.uint8, device=w.device)
+    if scales is None:
+        scales = torch.empty(rows, dtype=torch.float32, device=w.device)
+    N.check(N.lib().qi_fp8_quantize_rows(_ptr(w), rows, k, _ptr(q), _ptr(scales), _stream(w.device)),
+            "qi_fp8_quantize_rows")
+    return q, scales
