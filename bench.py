@@ -1,0 +1,381 @@
+"""Bank-latency benchmark of the folded-VPP long-context prefill on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one bank: R requests x L prompt tokens (default 4 x 32768) of the
+27B-shaped NVFP4 decoder, chunk 2048, through 2N virtual stages folded onto N
+GPUs (one process per GPU, launched by torchrun for N > 1).  Prints one JSON
+line on rank 0.  Inputs: seeded synthetic embeddings and random-init weights
+of the architecture (no checkpoint); the weights (~16 GB NVFP4) and KV pages
+exceed L2, so no extra flush is needed between banks.
+
+``--impl reference`` times the reference semantics on the host CPU instead:
+the repository's CPU restatement of the path (``oracle/``), one layer x one
+chunk at two history lengths, extrapolated to the whole bank (the reference
+has no CPU implementation of its own; its layer math runs in vLLM/FlashInfer
+GPU kernels built for sm_120).
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+import __graft_entry__  # noqa: E402
+
+METRIC = "4-request prefill bank latency & tok/s at 1/2/4/8 B200; % of NVFP4 TC peak"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=2)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--model", choices=("qwen27b", "tiny"), default="qwen27b")
+    p.add_argument("--requests", type=int, default=4)
+    p.add_argument("--prompt-tokens", type=int, default=32768)
+    p.add_argument("--chunk-size", type=int, default=2048)
+    p.add_argument("--transport", choices=("p2p", "nccl"), default="p2p")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-kernel-timing", action="store_true")
+    p.add_argument("--layers", type=int, default=None, help="override layer count (must split into 2N stages)")
+    return p.parse_args()
+
+
+def load_peaks():
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        peaks = json.loads(path.read_text())
+        return peaks, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock / throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, path):
+        self.path = Path(path)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.path.parent.mkdir(parents=True, exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[1]), max=float(parts[2]), power=float(parts[3]),
+                                 hw=parts[5], hwt=parts[6], swt=parts[7], pcap=parts[8]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        loaded = [r for r in rows if r["power"] > 300] or rows
+        reasons = set()
+        for r in loaded:
+            for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"), ("swt", "sw_thermal_slowdown"),
+                              ("pcap", "sw_power_cap")):
+                if r[key].lower().startswith("active"):
+                    reasons.add(name)
+        return dict(sm_mhz=statistics.median(r["sm"] for r in loaded), sm_max_mhz=max(r["max"] for r in loaded),
+                    reasons=sorted(reasons), samples=len(loaded))
+
+
+# ---------------------------------------------------------------------------
+# CPU legs: the oracle (CPU restatement of the reference semantics)
+# ---------------------------------------------------------------------------
+
+def cpu_sample(args, threads):
+    """Time the oracle's layer forward for one chunk at history 0 and at the
+    longest history of the bank; extrapolate to a bank by the cost model
+    t(h) = a + b * attention_pairs(h) summed over every chunk and layer."""
+    import numpy as np
+    import torch
+    from oracle import model as OM
+
+    torch.set_num_threads(threads)
+    shape = OM.QWEN27B if args.model == "qwen27b" else OM.TINY
+    layers = args.layers or shape.layers
+    c = args.chunk_size
+    hist_long = max(0, (args.prompt_tokens - 1) // c * c)
+    max_tokens = hist_long + c
+    m = OM.OracleModel(shape, [0], max_tokens)
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((c, shape.hidden)).astype(np.float32)
+    from oracle import formats as F
+
+    x = F.bf16_round(x)
+    times = {}
+    for hist in (0, hist_long):
+        t0 = time.perf_counter()
+        m.layer(0, x, x, hist)
+        times[hist] = time.perf_counter() - t0
+
+    def pairs(h, rows):
+        return rows * h + rows * (rows + 1) // 2
+
+    p0, p1 = pairs(0, c), pairs(hist_long, c)
+    b = (times[hist_long] - times[0]) / (p1 - p0) if p1 > p0 else 0.0
+    a = times[0] - b * p0
+    total = 0.0
+    for r in range(args.requests):
+        for start in range(0, args.prompt_tokens, c):
+            rows = min(c, args.prompt_tokens - start)
+            total += (a * rows / c + b * pairs(start, rows)) * layers
+    tokens = args.requests * args.prompt_tokens
+    sample = (f"oracle layer forward, 1 layer x {c} rows at history 0 and {hist_long} "
+              f"({times[0]:.1f} s + {times[hist_long]:.1f} s), extrapolated to {args.requests}x{args.prompt_tokens} "
+              f"tokens x {layers} layers (extrapolated)")
+    return dict(value=tokens / total, unit="tok/s", cores=threads, kind="port", sample=sample,
+                bank_seconds=total)
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    steps = []
+    base = None
+    for _ in range(max(1, args.steps)):
+        base = cpu_sample(args, threads)
+        steps.append(base["bank_seconds"])
+    bank_s = statistics.median(steps)
+    tokens = args.requests * args.prompt_tokens
+    value = tokens / bank_s
+    line = dict(
+        metric=METRIC, value=value, unit="tok/s", n_gpus=args.gpus, steps=args.steps, warmup=args.warmup,
+        ms_per_step=bank_s * 1e3, higher_is_better=True, scaling="strong", vs_baseline=None, dtype="f32",
+        data="synthetic", impl="reference",
+        config=dict(workload=f"{args.model} {args.requests}x{args.prompt_tokens} chunk {args.chunk_size}",
+                    model=args.model, requests=args.requests, prompt_tokens=args.prompt_tokens,
+                    chunk=args.chunk_size),
+        cpu_baseline=dict(value=value, unit="tok/s", cores=threads, kind="port", sample=base["sample"]),
+        e2e=dict(value=value, unit="tok/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0),
+    )
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    __graft_entry__.load_package()
+    from qwen_infra_b200 import kernels as K
+    from qwen_infra_b200.vpp import model as M
+    from qwen_infra_b200.vpp.runner import FoldedRank
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    shape = M.SHAPES[args.model]
+    if args.layers:
+        shape = M.ModelShape(args.layers, shape.hidden, shape.qheads, shape.kvheads, shape.head_dim,
+                             shape.intermediate)
+    transport = None
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+        from qwen_infra_b200.vpp.stages import StageBoundaries
+
+        transport = StageBoundaries(rank, world, dev, args.chunk_size, shape.hidden, backend=args.transport)
+    request_tokens = [args.prompt_tokens] * args.requests
+    runner = FoldedRank(shape, rank, world, dev, request_tokens, args.chunk_size, transport=transport)
+    gen = torch.Generator(device=dev).manual_seed(4321)
+    embeds = [torch.randn(t, shape.hidden, generator=gen, device=dev).to(torch.bfloat16) for t in request_tokens] \
+        if rank == 0 else None
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        runner.run_bank(embeds)
+    torch.cuda.synchronize()
+    runner.model.check_status()
+
+    # --- timed: inputs resident in HBM -----------------------------------
+    sampler = ClockSampler(REPO / "gpurun_out" / f"clocks_rank{rank}.csv") if rank == 0 else None
+    prof = K.LaunchProfile(timing=not args.no_kernel_timing)
+    K.PROFILE = prof
+    barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        runner.run_bank(embeds)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    K.PROFILE = None
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    launches_per_step = prof.launches / args.steps
+    kernel_summary = prof.summary()
+    runner.model.check_status()
+
+    # --- bubble: one instrumented bank with per-stage events ---------------
+    barrier()
+    torch.cuda.synchronize()
+    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    b0.record(stream)
+    runner.run_bank(embeds, record_events=True)
+    b1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    makespan = max_over_ranks(b0.elapsed_time(b1))
+    busiest = max_over_ranks(runner.compute_ms())
+    bubble = max(0.0, (makespan - busiest) / makespan)
+
+    # --- e2e: host embeddings copied in, result copied out, every bank ----
+    e2e = None
+    if not args.no_e2e:
+        host = [e.cpu().pin_memory() for e in embeds] if rank == 0 else None
+        out_host = torch.empty((args.requests, shape.hidden), dtype=torch.bfloat16).pin_memory()
+        runner.run_bank(None, host_embeds=host)
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            last = runner.run_bank(None, host_embeds=host)
+            if rank == 0:
+                out_host.copy_(last, non_blocking=True)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
+        tokens = args.requests * args.prompt_tokens
+        e2e = dict(value=tokens / (e2e_ms / 1e3), unit="tok/s", ms_per_step=e2e_ms,
+                   h2d_bytes_per_step=tokens * shape.hidden * 2, d2h_bytes_per_step=args.requests * shape.hidden * 2)
+
+    if rank != 0:
+        if transport is not None:
+            transport.close()
+        dist.destroy_process_group()
+        return 0
+
+    tokens = args.requests * args.prompt_tokens
+    peaks, peak_kind = load_peaks()
+    total_flops = tokens * shape.linear_flops_per_token() * shape.layers
+    for r in range(args.requests):
+        for start in range(0, args.prompt_tokens, args.chunk_size):
+            rows = min(args.chunk_size, args.prompt_tokens - start)
+            total_flops += shape.attention_flops(start, rows) * shape.layers
+    kernels = {}
+    for name, d in kernel_summary.items():
+        avg_ms = d["ms"] / d["launches"]
+        rate = d["work"] / (d["ms"] / 1e3)
+        kernels[name] = dict(launches_per_step=d["launches"] / args.steps, ms_per_step=d["ms"] / args.steps,
+                             share=None, achieved=(rate / 1e12 if d["unit"] == "FLOP" else rate / 1e9),
+                             unit=("TFLOP/s" if d["unit"] == "FLOP" else "GB/s"), avg_launch_ms=avg_ms)
+    ksum = sum(k["ms_per_step"] for k in kernels.values()) or 1.0
+    for k in kernels.values():
+        k["share"] = k["ms_per_step"] / ksum
+    roofline = None
+    if kernels:
+        dom_name = max(kernels, key=lambda n: kernels[n]["ms_per_step"])
+        dom = kernels[dom_name]
+        if dom["unit"] == "GB/s":
+            peak, pk = peaks["hbm_gbs"], f"hbm_gbs ({peak_kind})"
+            bound = "hbm"
+        elif dom_name == "gemm_nvfp4":
+            peak, pk = 4 * peaks["bf16_tflops"], f"4 x bf16_tflops ({peak_kind}; dense NVFP4:BF16 = 4:1 nominal)"
+            bound = "tensor"
+        elif dom_name == "gemm_e4m3":
+            peak, pk = 2 * peaks["bf16_tflops"], f"2 x bf16_tflops ({peak_kind}; dense FP8:BF16 = 2:1 nominal)"
+            bound = "tensor"
+        else:
+            peak, pk = peaks["bf16_tflops"], f"bf16_tflops ({peak_kind})"
+            bound = "tensor"
+        roofline = dict(kernel=dom_name, bound=bound, achieved=dom["achieved"], peak=peak, unit=dom["unit"],
+                        frac=dom["achieved"] / peak, peak_source=pk, traffic=None)
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_sample(args, os.cpu_count() or 1)
+        cpu.pop("bank_seconds", None)
+    line = dict(
+        metric=METRIC, value=tokens / (ms / 1e3), unit="tok/s", n_gpus=world, steps=args.steps,
+        warmup=args.warmup, ms_per_step=ms, bank_latency_ms=ms, higher_is_better=True, scaling="strong",
+        vs_baseline=None, dtype="nvfp4 (e2m1 x e4m3/16, fp32 accum), fp8 O-proj, bf16 attention",
+        data="synthetic (seeded embeddings, random-init weights of the architecture)",
+        config=dict(workload=f"{args.model} {args.requests}x{args.prompt_tokens} tokens, chunk {args.chunk_size}, "
+                             f"{2 * world} virtual stages on {world} GPU(s)",
+                    model=args.model, layers=shape.layers, requests=args.requests,
+                    prompt_tokens=args.prompt_tokens, chunk=args.chunk_size, virtual_stages=2 * world,
+                    parallelism=f"folded-vpp pp{world}", transport=(args.transport if world > 1 else "local fold"),
+                    l2="inputs larger than L2 (weights ~16 GB, KV pages)"),
+        bubble_fraction=bubble, busiest_rank_compute_ms=busiest, model_tflops=total_flops / (ms / 1e3) / 1e12,
+        gpu_launches=int(launches_per_step * args.steps), kernels=kernels, roofline=roofline, clocks=clocks,
+        e2e=e2e, cpu_baseline=cpu,
+    )
+    print(json.dumps(line), flush=True)
+    if transport is not None:
+        transport.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -58,13 +58,27 @@ def _round_to_grid(a, grid):
     return np.where(take_hi, hi, lo).astype(np.int64)
 
 
-def e2m1_encode(x):
-    """float32 array -> uint8 codes 0..15 (one code per element)."""
+def e2m1_encode_grid(x):
+    """float32 array -> uint8 codes 0..15 by nearest-even search on the grid."""
     x = np.asarray(x, dtype=np.float32)
     a = np.abs(x).astype(np.float64)
     code = _round_to_grid(a, E2M1_VALUES)
     sign = np.signbit(x).astype(np.int64) << 3
     return (code | sign).astype(np.uint8)
+
+
+def e2m1_encode(x):
+    """float32 array -> uint8 codes 0..15 (one code per element).
+
+    Same result as :func:`e2m1_encode_grid`, written as the count of decision
+    thresholds passed: the midpoints 0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5 of
+    neighbouring codes, where a tie goes to the even code (strict '>' when the
+    lower neighbour is even, '>=' when the upper one is)."""
+    x = np.asarray(x, dtype=np.float32)
+    a = np.abs(x)
+    code = ((a > 0.25).astype(np.uint8) + (a >= 0.75) + (a > 1.25) + (a >= 1.75) + (a > 2.5) + (a >= 3.5)
+            + (a > 5.0)).astype(np.uint8)
+    return (code | (np.signbit(x).astype(np.uint8) << 3)).astype(np.uint8)
 
 
 def e2m1_decode(codes):

@@ -146,18 +146,22 @@ class KVCache:
 
 def attention(q, k, v, history, shape):
     """Causal GQA softmax(Q K^T / sqrt(D)) V in fp32 for one chunk of queries
-    at positions history .. history+rows-1 over keys 0 .. history+rows-1."""
+    at positions history .. history+rows-1 over keys 0 .. history+rows-1.
+    Heads are processed a few at a time to bound the score matrix."""
     s = shape
     rows = q.shape[0]
+    group = s.qheads // s.kvheads
     qt = torch.from_numpy(np.ascontiguousarray(q)).view(rows, s.qheads, s.head_dim).transpose(0, 1)
-    kt = torch.from_numpy(k).transpose(0, 1).repeat_interleave(s.qheads // s.kvheads, 0)
-    vt = torch.from_numpy(v).transpose(0, 1).repeat_interleave(s.qheads // s.kvheads, 0)
-    scores = torch.matmul(qt, kt.transpose(1, 2)) / float(np.sqrt(s.head_dim))
+    kt = torch.from_numpy(np.ascontiguousarray(k)).transpose(0, 1)  # [Hkv, T, D]
+    vt = torch.from_numpy(np.ascontiguousarray(v)).transpose(0, 1)
     qpos = torch.arange(rows)[:, None] + history
     kpos = torch.arange(k.shape[0])[None, :]
-    scores = scores.masked_fill(kpos > qpos, float("-inf"))
-    p = torch.softmax(scores, dim=-1)
-    out = torch.matmul(p, vt)  # [Hq, rows, D]
+    mask = kpos > qpos
+    out = torch.empty(s.qheads, rows, s.head_dim)
+    for h in range(s.qheads):
+        scores = torch.matmul(qt[h], kt[h // group].T) / float(np.sqrt(s.head_dim))
+        scores = scores.masked_fill(mask, float("-inf"))
+        out[h] = torch.matmul(torch.softmax(scores, dim=-1), vt[h // group])
     return out.transpose(0, 1).reshape(rows, s.qheads * s.head_dim).numpy()
 
 

@@ -15,6 +15,49 @@ import torch
 from . import _native as N
 
 
+class LaunchProfile:
+    """Optional launch accounting: counts every kernel entry point called and,
+    when ``timing`` is set, brackets each launch with CUDA events on the
+    launching stream together with its algorithmic work (FLOPs or bytes)."""
+
+    def __init__(self, timing=False):
+        self.timing = timing
+        self.launches = 0
+        self.records = []  # (name, work, unit, start_event, end_event)
+
+    def launch(self, name, work, unit, stream_dev, fn):
+        self.launches += 1
+        if not self.timing:
+            return fn()
+        stream = torch.cuda.current_stream(stream_dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        rc = fn()
+        e1.record(stream)
+        self.records.append((name, work, unit, e0, e1))
+        return rc
+
+    def summary(self):
+        """{name: dict(launches, ms, work, unit)} over the recorded launches."""
+        out = {}
+        for name, work, unit, e0, e1 in self.records:
+            d = out.setdefault(name, dict(launches=0, ms=0.0, work=0.0, unit=unit))
+            d["launches"] += 1
+            d["ms"] += e0.elapsed_time(e1)
+            d["work"] += work
+        return out
+
+
+PROFILE = None
+
+
+def _run(name, work, unit, dev, fn):
+    if PROFILE is None:
+        return fn()
+    return PROFILE.launch(name, work, unit, dev, fn)
+
+
 def _ptr(t):
     return None if t is None else ct.c_void_p(t.data_ptr())
 
@@ -55,8 +98,8 @@ def norm_pack(x, residual, gamma, global_scale, *, eps=1e-6, weight_offset=1.0, 
         scales = torch.empty(scale_buffer_bytes(rows, h), dtype=torch.uint8, device=x.device)
     if updated is None and want_updated:
         updated = torch.empty_like(x)
-    N.check(N.lib().qi_norm_pack(_ptr(x), _ptr(residual), _ptr(gamma), _ptr(global_scale), _ptr(q), _ptr(scales),
-                                 _ptr(updated), rows, h, eps, weight_offset, _stream(x.device)), "qi_norm_pack")
+    N.check(_run("norm_pack", rows * (h * 2 * (2 if residual is not None else 1) + (2 * h if updated is not None else 0) + h // 2 + h // 16), "B", x.device, lambda: N.lib().qi_norm_pack(_ptr(x), _ptr(residual), _ptr(gamma), _ptr(global_scale), _ptr(q), _ptr(scales),
+                                 _ptr(updated), rows, h, eps, weight_offset, _stream(x.device))), "qi_norm_pack")
     return q, scales, updated
 
 
@@ -65,8 +108,8 @@ def rms_norm(x, residual, gamma, *, eps=1e-6, weight_offset=1.0, out=None, updat
     rows, h = x.shape
     if out is None:
         out = torch.empty_like(x)
-    N.check(N.lib().qi_rms_norm(_ptr(x), _ptr(residual), _ptr(gamma), _ptr(out), _ptr(updated), rows, h, eps,
-                                weight_offset, _stream(x.device)), "qi_rms_norm")
+    N.check(_run("rms_norm", rows * h * 2 * (3 if residual is not None else 2), "B", x.device, lambda: N.lib().qi_rms_norm(_ptr(x), _ptr(residual), _ptr(gamma), _ptr(out), _ptr(updated), rows, h, eps,
+                                weight_offset, _stream(x.device))), "qi_rms_norm")
     return out
 
 
@@ -132,7 +175,7 @@ def qk_rope_kv_append(qkv, positions, q_weight, k_weight, cos_sin, slots, kv, k_
     p.data_page, p.data_row, p.data_head = kv.k.stride(0), kv.k.stride(1), kv.k.stride(2)
     p.sf_page, p.sf_row, p.sf_head = kv.ks.stride(0), kv.ks.stride(1), kv.ks.stride(2)
     p.eps, p.weight_offset = eps, weight_offset
-    N.check(N.lib().qi_qk_rope_kv_append(ct.byref(p), _stream(qkv.device)), "qi_qk_rope_kv_append")
+    N.check(_run("qk_rope_kv_append", rows * (qkv.shape[1] * 2 + 2 * qheads * d * 2 + kvheads * (d + d // 8) + d * 4), "B", qkv.device, lambda: N.lib().qi_qk_rope_kv_append(ct.byref(p), _stream(qkv.device))), "qi_qk_rope_kv_append")
     return q, gate
 
 
@@ -144,8 +187,8 @@ def gate_fp8(out, gate, *, fp8=None, scale=None):
         fp8 = torch.empty((rows, cols), dtype=torch.uint8, device=out.device)
     if scale is None:
         scale = torch.empty(rows, dtype=torch.float32, device=out.device)
-    N.check(N.lib().qi_gate_fp8(_ptr(out), _ptr(gate), out.stride(0), gate.stride(0), _ptr(fp8), fp8.stride(0),
-                                _ptr(scale), rows, cols, _stream(out.device)), "qi_gate_fp8")
+    N.check(_run("gate_fp8", rows * (cols * 5 + 4), "B", out.device, lambda: N.lib().qi_gate_fp8(_ptr(out), _ptr(gate), out.stride(0), gate.stride(0), _ptr(fp8), fp8.stride(0),
+                                _ptr(scale), rows, cols, _stream(out.device))), "qi_gate_fp8")
     return fp8, scale
 
 
@@ -168,7 +211,7 @@ def gemm_nvfp4(a, sfa, b, sfb, *, m, n, k, alpha=None, alpha_value=1.0, out=None
         out = torch.empty((m, n), dtype=out_dtype, device=a.device)
     g = _gemm_struct(N.GEMM_NVFP4, epi, m, n, k, a, b, sfa, sfb, alpha, alpha_value)
     g.out, g.ldo = out.data_ptr(), out.stride(0)
-    N.check(N.lib().qi_gemm(ct.byref(g), _stream(a.device)), "qi_gemm")
+    N.check(_run("gemm_nvfp4" if g.kind == N.GEMM_NVFP4 else "gemm_e4m3", 2.0 * m * n * k, "FLOP", a.device, lambda: N.lib().qi_gemm(ct.byref(g), _stream(a.device))), "qi_gemm")
     return out
 
 
@@ -184,7 +227,7 @@ def gemm_swiglu_nvfp4(a, sfa, b, sfb, act_global, *, m, n, k, alpha=None, alpha_
         act_sf = torch.empty(scale_buffer_bytes(m, inter), dtype=torch.uint8, device=a.device)
     g = _gemm_struct(N.GEMM_NVFP4, N.EPI_SWIGLU_NVFP4, m, n, k, a, b, sfa, sfb, alpha, alpha_value)
     g.act_q, g.act_sf, g.act_global, g.act_ld = act_q.data_ptr(), act_sf.data_ptr(), act_global.data_ptr(), act_q.stride(0)
-    N.check(N.lib().qi_gemm(ct.byref(g), _stream(a.device)), "qi_gemm")
+    N.check(_run("gemm_nvfp4" if g.kind == N.GEMM_NVFP4 else "gemm_e4m3", 2.0 * m * n * k, "FLOP", a.device, lambda: N.lib().qi_gemm(ct.byref(g), _stream(a.device))), "qi_gemm")
     return act_q, act_sf
 
 
@@ -203,7 +246,7 @@ def gemm_e4m3(a, b, *, m, n, k, row_scale=None, col_scale=None, alpha_value=1.0,
     g.row_scale = row_scale.data_ptr() if row_scale is not None else None
     g.col_scale = col_scale.data_ptr() if col_scale is not None else None
     g.out, g.ldo = out.data_ptr(), out.stride(0)
-    N.check(N.lib().qi_gemm(ct.byref(g), _stream(a.device)), "qi_gemm")
+    N.check(_run("gemm_nvfp4" if g.kind == N.GEMM_NVFP4 else "gemm_e4m3", 2.0 * m * n * k, "FLOP", a.device, lambda: N.lib().qi_gemm(ct.byref(g), _stream(a.device))), "qi_gemm")
     return out
 
 
@@ -218,8 +261,8 @@ def kv_dequant(kv, block_table, tokens, *, k_out=None, vt_out=None):
     if vt_out is None:
         vt_out = torch.empty((kv.kvheads, d, vt_row), dtype=torch.bfloat16, device=kv.k.device)
     view = kv.view()
-    N.check(N.lib().qi_kv_dequant(ct.byref(view), _ptr(block_table), tokens, _ptr(k_out), _ptr(vt_out), vt_row,
-                                  _stream(kv.k.device)), "qi_kv_dequant")
+    N.check(_run("kv_dequant", tokens * kv.kvheads * (d + d // 8 + 4 * d), "B", kv.k.device, lambda: N.lib().qi_kv_dequant(ct.byref(view), _ptr(block_table), tokens, _ptr(k_out), _ptr(vt_out), vt_row,
+                                  _stream(kv.k.device))), "qi_kv_dequant")
     return k_out, vt_out
 
 
@@ -240,7 +283,7 @@ def prefill_attention(q, k, vt, *, history, qheads, kvheads, head_dim, k_global,
     p.qheads, p.kvheads, p.head_dim = qheads, kvheads, head_dim
     p.q_row, p.out_row, p.vt_row = q.stride(0), out.stride(0), vt.shape[2]
     p.softmax_scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(head_dim)
-    N.check(N.lib().qi_prefill_attention(ct.byref(p), _stream(q.device)), "qi_prefill_attention")
+    N.check(_run("attention", 4 * qheads * head_dim * (rows * history + rows * (rows + 1) // 2), "FLOP", q.device, lambda: N.lib().qi_prefill_attention(ct.byref(p), _stream(q.device))), "qi_prefill_attention")
     return out
 
 
@@ -254,8 +297,8 @@ def nvfp4_quantize(w, global_scale, *, q=None, scales=None):
         q = torch.empty((rows, k // 2), dtype=torch.uint8, device=w.device)
     if scales is None:
         scales = torch.zeros(scale_buffer_bytes(rows, k), dtype=torch.uint8, device=w.device)
-    N.check(N.lib().qi_nvfp4_quantize(_ptr(w), rows, k, _ptr(global_scale), _ptr(q), _ptr(scales),
-                                      _stream(w.device)), "qi_nvfp4_quantize")
+    N.check(_run("nvfp4_quantize", rows * k * 4, "B", w.device, lambda: N.lib().qi_nvfp4_quantize(_ptr(w), rows, k, _ptr(global_scale), _ptr(q), _ptr(scales),
+                                      _stream(w.device))), "qi_nvfp4_quantize")
     return q, scales
 
 
@@ -266,6 +309,5 @@ def fp8_quantize_rows(w, *, q=None, scales=None):
         q = torch.empty((rows, k), dtype=torch.uint8, device=w.device)
     if scales is None:
         scales = torch.empty(rows, dtype=torch.float32, device=w.device)
-    N.check(N.lib().qi_fp8_quantize_rows(_ptr(w), rows, k, _ptr(q), _ptr(scales), _stream(w.device)),
-            "qi_fp8_quantize_rows")
+    N.check(_run("fp8_quantize_rows", rows * k * 5, "B", w.device, lambda: N.lib().qi_fp8_quantize_rows(_ptr(w), rows, k, _ptr(q), _ptr(scales), _stream(w.device))), "qi_fp8_quantize_rows")
     return q, scales

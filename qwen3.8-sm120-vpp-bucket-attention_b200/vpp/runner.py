@@ -1,0 +1,120 @@
+"""Bank driver of one rank of the folded pipeline (one process per GPU).
+
+A bank is R requests of prompt tokens, cut into chunks of at most C tokens
+(request-major, as a first-come-first-served chunked-prefill scheduler would
+issue them); every chunk is one batch that flows through the 2G virtual stages.
+Each rank runs its precomputed stage order (``layout.rank_local_stage_orders``,
+the same order the reference's executor messages produce,
+``src/qwen_infra/vpp/executor.py:15-73`` / ``worker.py:117-183``):
+
+    receive (or local fold) -> run the stage's layers -> send -> retire
+
+Per-stage FIFO order makes the KV history of chunk j+1 ready when it reaches
+a layer: chunk j passed the same stage, on the same stream, before it.
+"""
+
+from dataclasses import dataclass
+
+import torch
+
+from . import layout as L
+from .model import StageModel
+
+
+@dataclass(frozen=True)
+class Chunk:
+    batch: int
+    request: int
+    start: int
+    rows: int
+
+
+def plan_bank(request_tokens, chunk):
+    chunks = []
+    for r, tokens in enumerate(request_tokens):
+        for start in range(0, tokens, chunk):
+            chunks.append(Chunk(len(chunks), r, start, min(chunk, tokens - start)))
+    return chunks
+
+
+class FoldedRank:
+    """Rank ``rank`` of ``ranks``: owns stages rank and 2G-1-rank."""
+
+    def __init__(self, shape, rank, ranks, device, request_tokens, chunk, *, transport=None, base_seed=1234,
+                 on_device_init=None, keep_all_outputs=False):
+        self.shape, self.rank, self.ranks = shape, rank, ranks
+        self.device = torch.device(device)
+        self.request_tokens = list(request_tokens)
+        self.chunk = chunk
+        self.spans = L.layer_ranges(rank, ranks, shape.layers)
+        layers = list(range(*self.spans[0])) + list(range(*self.spans[1]))
+        self.model = StageModel(shape, layers, self.device, max_rows=chunk, request_tokens=self.request_tokens,
+                                base_seed=base_seed, on_device_init=on_device_init, final_norm=(rank == 0))
+        self.transport = transport
+        self.chunks = plan_bank(self.request_tokens, chunk)
+        self.order = L.rank_local_stage_orders([c.batch for c in self.chunks], ranks)[rank]
+        self.keep_all_outputs = keep_all_outputs
+        h = shape.hidden
+        self.fold = (torch.empty((chunk, h), dtype=torch.bfloat16, device=self.device),
+                     torch.empty((chunk, h), dtype=torch.bfloat16, device=self.device))
+        self.last_hidden = torch.empty((len(self.request_tokens), h), dtype=torch.bfloat16, device=self.device)
+        self.outputs = {}
+        self.contexts = None
+        self.stage_events = []
+
+    def _contexts(self):
+        if self.contexts is None:
+            self.contexts = [self.model.chunk_context(c.request, c.start, c.rows) for c in self.chunks]
+        return self.contexts
+
+    def run_bank(self, embeds, *, host_embeds=None, record_events=False):
+        """Run this rank's ops for one bank.  ``embeds``: device bf16 [tokens, H]
+        per request (list), or None with ``host_embeds`` (pinned host tensors,
+        copied chunk by chunk inside the run)."""
+        G = self.ranks
+        last_stage = 2 * G - 1
+        ctxs = self._contexts()
+        stream = torch.cuda.current_stream(self.device)
+        self.stage_events = []
+        for batch, stage in self.order:
+            ch = self.chunks[batch]
+            ctx = ctxs[batch]
+            if record_events:
+                ev0 = torch.cuda.Event(enable_timing=True)
+                ev0.record(stream)
+            if stage == 0:
+                if host_embeds is not None:
+                    hidden = host_embeds[ch.request][ch.start:ch.start + ch.rows].to(self.device, non_blocking=True)
+                else:
+                    hidden = embeds[ch.request][ch.start:ch.start + ch.rows]
+                residual = None
+            elif stage == G:  # local fold: stage G-1 ran on this rank just before
+                hidden, residual = self.fold[0][:ch.rows], self.fold[1][:ch.rows]
+            else:
+                hidden, residual = self.transport.receive(batch, stage, ch.rows)
+            span = L.stage_layers(stage, G, self.shape.layers)
+            if stage == G - 1:
+                out_planes = (self.fold[0][:ch.rows], self.fold[1][:ch.rows])
+            elif stage == last_stage:
+                out_planes = None
+            else:
+                out_planes = self.transport.prepare_send(batch, stage, ch.rows)
+            h, r = self.model.run_layers(span, hidden, residual, ctx, out_planes)
+            if stage not in (G - 1, last_stage):
+                self.transport.send(batch, stage, ch.rows)
+            if stage not in (0, G):
+                self.transport.retire(batch, stage)
+            if stage == last_stage:
+                if self.keep_all_outputs:
+                    self.outputs[batch] = self.model.final_norm(h, r)
+                elif ch.start + ch.rows == self.request_tokens[ch.request]:
+                    self.model.final_norm(h[-1:], r[-1:], out=self.last_hidden[ch.request:ch.request + 1])
+            if record_events:
+                ev1 = torch.cuda.Event(enable_timing=True)
+                ev1.record(stream)
+                self.stage_events.append((batch, stage, ev0, ev1))
+        return self.last_hidden
+
+    def compute_ms(self):
+        """Summed device time of this rank's stages in the last recorded bank."""
+        return sum(e0.elapsed_time(e1) for _, _, e0, e1 in self.stage_events)
