@@ -306,12 +306,15 @@ int launch_attention(const QiAttention* a, cudaStream_t stream) {
   if (!make_map_bf16(&mq, a->q, 2, qd, qs, 128) || !make_map_bf16(&mk, a->k, 3, kd, ks, 128) ||
       !make_map_bf16(&mv, a->vt, 3, vd, vs, HD))
     return (int)cudaErrorInvalidValue;
-  static bool configured = false;
-  if (!configured) {
+  static bool configured[64] = {};
+  int cur_dev = 0;
+  cudaGetDevice(&cur_dev);
+  if (cur_dev < 0 || cur_dev >= 64) return (int)cudaErrorInvalidDevice;
+  if (!configured[cur_dev]) {
     const cudaError_t e =
         cudaFuncSetAttribute(attn_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, Geometry<HD>::SMEM);
     if (e != cudaSuccess) return (int)e;
-    configured = true;
+    configured[cur_dev] = true;
   }
   AttnParams p{};
   p.rows = a->rows;
@@ -333,6 +336,7 @@ int launch_attention(const QiAttention* a, cudaStream_t stream) {
 }  // namespace
 
 extern "C" int qi_prefill_attention(const QiAttention* a, cudaStream_t stream) {
+  QI_BIND(stream, a ? a->q : nullptr);
   if (!a || a->rows < 1 || a->history < 0 || (a->head_dim != 64 && a->head_dim != 128) || a->qheads < 1 ||
       a->kvheads < 1 || a->qheads % a->kvheads || !a->q || !a->k || !a->vt || !a->out || !a->k_global ||
       !a->v_global)

@@ -22,6 +22,34 @@ enum : int {
   kStatusBadSlot = 1 << 2,      // a KV slot outside the cache (reported, skipped)
 };
 
+// The kernel library links its own (static) CUDA runtime, whose current
+// device is independent of the caller's runtime.  Every entry point makes the
+// device of its stream (or, for a default stream, of its first operand)
+// current before it launches.
+inline cudaError_t bind_device(cudaStream_t stream, const void* operand) {
+  int dev = -1;
+  const uintptr_t h = reinterpret_cast<uintptr_t>(stream);
+  if (h > 2) {
+    const cudaError_t e = cudaStreamGetDevice(stream, &dev);
+    if (e != cudaSuccess) return e;
+  } else if (operand) {
+    cudaPointerAttributes attr{};
+    const cudaError_t e = cudaPointerGetAttributes(&attr, operand);
+    if (e != cudaSuccess) return e;
+    dev = attr.device;
+  }
+  if (dev < 0) return cudaSuccess;
+  int cur = -1;
+  cudaGetDevice(&cur);
+  return cur == dev ? cudaSuccess : cudaSetDevice(dev);
+}
+
+#define QI_BIND(stream, ptr)                                   \
+  do {                                                         \
+    const cudaError_t qi_bind_e = qi::bind_device(stream, ptr); \
+    if (qi_bind_e != cudaSuccess) return (int)qi_bind_e;       \
+  } while (0)
+
 QI_DEV void report(int* status, int code) {
   if (status) atomicOr(status, code);
 }

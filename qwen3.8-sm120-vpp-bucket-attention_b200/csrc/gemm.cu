@@ -257,12 +257,15 @@ bool make_map_u8(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_
 
 template <bool kFp4, int kEpi>
 int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, cudaStream_t stream) {
-  static bool configured = false;
-  if (!configured) {
+  static bool configured[64] = {};
+  int cur_dev = 0;
+  cudaGetDevice(&cur_dev);
+  if (cur_dev < 0 || cur_dev >= 64) return (int)cudaErrorInvalidDevice;
+  if (!configured[cur_dev]) {
     const cudaError_t e =
         cudaFuncSetAttribute(gemm_kernel<kFp4, kEpi>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return (int)e;
-    configured = true;
+    configured[cur_dev] = true;
   }
   const dim3 grid((p.m + BM - 1) / BM, p.n / BN);
   gemm_kernel<kFp4, kEpi><<<grid, 192, SMEM_BYTES, stream>>>(ma, mb, p);
@@ -276,6 +279,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 extern "C" {
 
 int qi_gemm(const QiGemm* g, cudaStream_t stream) {
+  QI_BIND(stream, g ? g->a : nullptr);
   if (!g || g->m < 1 || g->n < BN || g->n % BN || !g->a || !g->b) return (int)cudaErrorInvalidValue;
   const bool fp4 = g->kind == QI_GEMM_NVFP4;
   if (!fp4 && g->kind != QI_GEMM_E4M3) return (int)cudaErrorInvalidValue;

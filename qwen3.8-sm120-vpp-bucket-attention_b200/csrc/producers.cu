@@ -405,6 +405,7 @@ extern "C" {
 int qi_norm_pack(const void* x, const void* residual, const void* gamma, const float* global_scale, void* q,
                  void* scales, void* updated, int rows, int hidden, float eps, float weight_offset,
                  cudaStream_t stream) {
+  QI_BIND(stream, x);
   if (rows < 1 || hidden < 64 || hidden % 64 || hidden > 16384 || !x || !gamma || !global_scale || !q || !scales)
     return (int)cudaErrorInvalidValue;
   if (!aligned16(x) || (residual && !aligned16(residual)) || (updated && !aligned16(updated)) || !aligned16(gamma) ||
@@ -420,6 +421,7 @@ int qi_norm_pack(const void* x, const void* residual, const void* gamma, const f
 
 int qi_rms_norm(const void* x, const void* residual, const void* gamma, void* out, void* updated, int rows,
                 int hidden, float eps, float weight_offset, cudaStream_t stream) {
+  QI_BIND(stream, x);
   if (rows < 1 || hidden < 64 || hidden % 64 || hidden > 16384 || !x || !gamma || !out)
     return (int)cudaErrorInvalidValue;
   if (!aligned16(x) || (residual && !aligned16(residual)) || !aligned16(out) || !aligned16(gamma) ||
@@ -452,6 +454,7 @@ int nvfp4_norm_pack_metadata(int* out) {
 }
 
 int qi_qk_rope_kv_append(const QiFront* p, cudaStream_t stream) {
+  QI_BIND(stream, p ? p->qkv : nullptr);
   if (!p || p->rows < 1 || p->qheads < 1 || p->kvheads < 1 || !p->qkv || !p->q_weight || !p->k_weight ||
       !p->cos_sin || !p->positions || !p->q || p->page_size < 1 || p->pages < 0)
     return (int)cudaErrorInvalidValue;
@@ -542,6 +545,7 @@ int nvfp4_attention_front_resources(int* out) {
 
 int qi_gate_fp8(const void* out, const void* gate, int64_t out_row, int64_t gate_row, void* fp8, int64_t fp8_row,
                 float* scale, int rows, int cols, cudaStream_t stream) {
+  QI_BIND(stream, out);
   if (rows < 1 || cols < 16 || cols % 16 || cols > 16384 || !out || !gate || !fp8 || !scale)
     return (int)cudaErrorInvalidValue;
   if (!aligned16(out) || !aligned16(gate) || !aligned16(fp8) || out_row % 8 || gate_row % 8 || fp8_row % 16)
@@ -555,6 +559,7 @@ int qi_gate_fp8(const void* out, const void* gate, int64_t out_row, int64_t gate
 
 int qi_nvfp4_quantize(const float* w, int64_t rows, int k, const float* global_scale, void* q, void* scales,
                       cudaStream_t stream) {
+  QI_BIND(stream, w);
   if (rows < 1 || k < 64 || k % 64 || !w || !global_scale || !q || !scales || !aligned16(w))
     return (int)cudaErrorInvalidValue;
   const int64_t work = rows * (k / 16);
@@ -567,6 +572,7 @@ int qi_nvfp4_quantize(const float* w, int64_t rows, int k, const float* global_s
 }
 
 int qi_fp8_quantize_rows(const float* w, int rows, int k, void* q, float* scales, cudaStream_t stream) {
+  QI_BIND(stream, w);
   if (rows < 1 || k < 1 || !w || !q || !scales) return (int)cudaErrorInvalidValue;
   fp8_rows_kernel<<<rows, 256, 0, stream>>>(w, k, static_cast<uint8_t*>(q), scales);
   return (int)cudaPeekAtLastError();
@@ -574,6 +580,7 @@ int qi_fp8_quantize_rows(const float* w, int rows, int k, void* q, float* scales
 
 int qi_kv_dequant(const QiKvView* kv, const int32_t* block_table, int tokens, void* k_out, void* vt_out,
                   int64_t vt_row, cudaStream_t stream) {
+  QI_BIND(stream, k_out);
   if (!kv || !block_table || tokens < 1 || !k_out || !vt_out || vt_row < tokens || vt_row % 64)
     return (int)cudaErrorInvalidValue;
   if (!kv->k_cache || !kv->v_cache || !kv->k_scales || !kv->v_scales || kv->kvheads < 1 || kv->page_size < 1)
@@ -596,6 +603,7 @@ int qi_kv_dequant(const QiKvView* kv, const int32_t* block_table, int tokens, vo
 }
 
 int qi_convert_probe(const float* in, void* e2m1_pairs, void* e4m3, float* ex, int n, cudaStream_t stream) {
+  QI_BIND(stream, in);
   if (!in || !e2m1_pairs || !e4m3 || !ex || n < 8 || n % 8) return (int)cudaErrorInvalidValue;
   convert_probe_kernel<<<(n + 255) / 256, 256, 0, stream>>>(in, static_cast<uint8_t*>(e2m1_pairs),
                                                              static_cast<uint8_t*>(e4m3), ex, n);

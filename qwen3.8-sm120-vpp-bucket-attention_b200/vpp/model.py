@@ -216,7 +216,7 @@ class StageModel:
         slots = bt[(pos // s.page_size).long()] * s.page_size + pos % s.page_size
         return ChunkContext(request, history, rows, pos, slots.to(torch.int32), bt)
 
-    def layer_forward(self, layer, hidden, residual, ctx, hidden_out, residual_out):
+    def layer_forward(self, layer, hidden, residual, ctx, hidden_out, residual_out, on_residual=None):
         s, ws, w = self.shape, self.ws, self.weights[layer]
         rows = ctx.rows
         h, d = s.hidden, s.head_dim
@@ -239,6 +239,8 @@ class StageModel:
                         out=ws.o[:rows])
         q_m, sf_m, _ = K.norm_pack(o, res1, w.ln_post, self.g_norm, eps=s.eps, q=ws.q_m[:rows], scales=ws.sf_m,
                                    updated=residual_out)
+        if on_residual is not None:
+            on_residual()  # the residual plane is final here; its transfer may start
         act_q, act_sf = K.gemm_swiglu_nvfp4(q_m, sf_m, w.gate_up.q, w.gate_up.sf, self.g_down, m=rows,
                                             n=2 * s.intermediate, k=h, alpha=w.alpha_gu, act_q=ws.act_q[:rows],
                                             act_sf=ws.act_sf)
@@ -246,7 +248,7 @@ class StageModel:
                      out=hidden_out)
         return hidden_out, residual_out
 
-    def run_layers(self, span, hidden, residual, ctx, out_planes=None):
+    def run_layers(self, span, hidden, residual, ctx, out_planes=None, on_residual=None):
         """Run layers [lo, hi) on one chunk.  ``out_planes`` = (hidden, residual)
         buffers that receive the final layer's output (e.g. a transport slot)."""
         lo, hi = span
@@ -258,7 +260,8 @@ class StageModel:
                 ho, ro = out_planes
             else:
                 ho, ro = ping[2 * (i % 2)], ping[2 * (i % 2) + 1]
-            hidden, residual = self.layer_forward(layer, hidden, residual, ctx, ho, ro)
+            hidden, residual = self.layer_forward(layer, hidden, residual, ctx, ho, ro,
+                                                  on_residual if last else None)
         return hidden, residual
 
     def final_norm(self, hidden, residual, out=None):

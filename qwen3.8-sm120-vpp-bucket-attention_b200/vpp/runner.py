@@ -76,6 +76,8 @@ class FoldedRank:
         ctxs = self._contexts()
         stream = torch.cuda.current_stream(self.device)
         self.stage_events = []
+        if self.transport is not None:
+            self.transport.set_order(self.order)
         for batch, stage in self.order:
             ch = self.chunks[batch]
             ctx = ctxs[batch]
@@ -93,13 +95,15 @@ class FoldedRank:
             else:
                 hidden, residual = self.transport.receive(batch, stage, ch.rows)
             span = L.stage_layers(stage, G, self.shape.layers)
+            on_residual = None
             if stage == G - 1:
                 out_planes = (self.fold[0][:ch.rows], self.fold[1][:ch.rows])
             elif stage == last_stage:
                 out_planes = None
             else:
                 out_planes = self.transport.prepare_send(batch, stage, ch.rows)
-            h, r = self.model.run_layers(span, hidden, residual, ctx, out_planes)
+                on_residual = (lambda b=batch, s=stage: self.transport.mark_residual_ready(b, s))
+            h, r = self.model.run_layers(span, hidden, residual, ctx, out_planes, on_residual)
             if stage not in (G - 1, last_stage):
                 self.transport.send(batch, stage, ch.rows)
             if stage not in (0, G):
