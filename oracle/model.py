@@ -144,24 +144,56 @@ class KVCache:
         return deq(self.k, self.ks, k_global), deq(self.v, self.vs, v_global)
 
 
-def attention(q, k, v, history, shape):
-    """Causal GQA softmax(Q K^T / sqrt(D)) V in fp32 for one chunk of queries
-    at positions history .. history+rows-1 over keys 0 .. history+rows-1.
-    Heads are processed a few at a time to bound the score matrix."""
+def attention(q, k, v, history, shape, tile=128):
+    """Causal GQA softmax(Q K^T / sqrt(D)) V for one chunk of queries at
+    positions history .. history+rows-1 over keys 0 .. history+rows-1, with
+    the reference's attention precision (bf16 Q/K/V operands, bf16 P for the
+    PV product, fp32 softmax statistics and accumulators) evaluated the way a
+    tiled prefill kernel evaluates it: keys in tiles of ``tile``, running row
+    max m, P = bf16(exp(s - m)), running sum l of the unrounded exponentials,
+    O rescaled by exp(m_old - m_new), output O / l."""
     s = shape
     rows = q.shape[0]
     group = s.qheads // s.kvheads
+    tokens = k.shape[0]
     qt = torch.from_numpy(np.ascontiguousarray(q)).view(rows, s.qheads, s.head_dim).transpose(0, 1)
     kt = torch.from_numpy(np.ascontiguousarray(k)).transpose(0, 1)  # [Hkv, T, D]
     vt = torch.from_numpy(np.ascontiguousarray(v)).transpose(0, 1)
     qpos = torch.arange(rows)[:, None] + history
-    kpos = torch.arange(k.shape[0])[None, :]
-    mask = kpos > qpos
+    scale = 1.0 / float(np.sqrt(s.head_dim))
     out = torch.empty(s.qheads, rows, s.head_dim)
     for h in range(s.qheads):
-        scores = torch.matmul(qt[h], kt[h // group].T) / float(np.sqrt(s.head_dim))
-        scores = scores.masked_fill(mask, float("-inf"))
-        out[h] = torch.matmul(torch.softmax(scores, dim=-1), vt[h // group])
+        m = torch.full((rows, 1), float("-inf"))
+        l = torch.zeros(rows, 1)
+        o = torch.zeros(rows, s.head_dim)
+        for t0 in range(0, tokens, tile):
+            kk = kt[h // group, t0:t0 + tile]
+            sc = torch.matmul(qt[h], kk.T) * scale
+            kpos = torch.arange(t0, t0 + kk.shape[0])[None, :]
+            sc = sc.masked_fill(kpos > qpos, float("-inf"))
+            m_new = torch.maximum(m, sc.max(dim=1, keepdim=True).values)
+            corr = torch.where(m == float("-inf"), torch.zeros_like(m), torch.exp(m - m_new))
+            e = torch.where(sc == float("-inf"), torch.zeros_like(sc), torch.exp(sc - m_new))
+            l = l * corr + e.sum(dim=1, keepdim=True)
+            o = o * corr + torch.matmul(e.to(torch.bfloat16).float(), vt[h // group, t0:t0 + tile])
+            m = m_new
+        out[h] = o / l
+    return out.transpose(0, 1).reshape(rows, s.qheads * s.head_dim).numpy()
+
+
+def attention_exact(q, k, v, history, shape):
+    """The same attention with fp32 P (no bf16 rounding), one pass per head."""
+    s = shape
+    rows = q.shape[0]
+    group = s.qheads // s.kvheads
+    qt = torch.from_numpy(np.ascontiguousarray(q)).view(rows, s.qheads, s.head_dim).transpose(0, 1)
+    kt = torch.from_numpy(np.ascontiguousarray(k)).transpose(0, 1)
+    vt = torch.from_numpy(np.ascontiguousarray(v)).transpose(0, 1)
+    mask = torch.arange(k.shape[0])[None, :] > (torch.arange(rows)[:, None] + history)
+    out = torch.empty(s.qheads, rows, s.head_dim)
+    for h in range(s.qheads):
+        sc = torch.matmul(qt[h], kt[h // group].T) / float(np.sqrt(s.head_dim))
+        out[h] = torch.matmul(torch.softmax(sc.masked_fill(mask, float("-inf")), dim=-1), vt[h // group])
     return out.transpose(0, 1).reshape(rows, s.qheads * s.head_dim).numpy()
 
 

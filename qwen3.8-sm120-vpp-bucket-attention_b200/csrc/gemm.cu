@@ -31,7 +31,10 @@ constexpr int SFB_BYTES = 4096;  // 256 rows x 16 scales
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t ACC_COL = 0, SFA_COL = 256, SFB_COL = 272;
+// Scale factors get their own TMEM columns per pipeline stage (16 for A, 32
+// for B), so copying the next stage's scales never waits on MMAs that still
+// read the previous ones.
+constexpr uint32_t ACC_COL = 0, SFA_COL = 256, SFB_COL = 256 + STAGES * 16;
 
 struct Params {
   int m, n, kt;  // kt: number of 128-byte K tiles
@@ -124,7 +127,7 @@ __global__ void __launch_bounds__(192, 1)
           const uint64_t bdesc = sdesc_kmajor_sw128(b_base + kk * 32);
           const uint32_t acc = (kt | kk) ? 1u : 0u;
           if constexpr (kFp4) {
-            const uint32_t sfa_t = tmem + SFA_COL + kk * 4, sfb_t = tmem + SFB_COL + kk * 8;
+            const uint32_t sfa_t = tmem + SFA_COL + s * 16 + kk * 4, sfb_t = tmem + SFB_COL + s * 32 + kk * 8;
             tc_cp_sf(sfa_t, sdesc_sf_atom(smem_u32(sSFA + s * SFA_BYTES + kk * 512)));
             tc_cp_sf(sfb_t, sdesc_sf_atom(smem_u32(sSFB + s * SFB_BYTES + kk * 512)));
             tc_cp_sf(sfb_t + 4, sdesc_sf_atom(smem_u32(sSFB + s * SFB_BYTES + 2048 + kk * 512)));
