@@ -199,6 +199,25 @@ class StageBoundaries:
         self.ctrl_in[stage].grant(seq, p)
         self.grant_seq[stage] += 1
 
+    def _wait_progressing(self, what, attempt, slice_s=2e-4):
+        """Wait for ``attempt`` (a short bounded native wait that raises
+        TransportTimeout when its slice runs out) while still granting credits
+        and retiring slots: a rank blocked here must not stop serving its
+        peers, or two ranks waiting on each other's credits would deadlock."""
+        deadline = time.monotonic() + self.timeout
+        while True:
+            try:
+                return attempt(slice_s)
+            except NV.TransportTimeout:
+                pass
+            except NV.PeerFailed:
+                self._fail()
+                raise
+            self.progress()
+            if time.monotonic() > deadline:
+                self._fail()
+                raise NV.TransportTimeout(f"deadline passed waiting for {what}")
+
     def _deadline_loop(self, what, ready):
         deadline = time.monotonic() + self.timeout
         spins = 0
@@ -250,11 +269,9 @@ class StageBoundaries:
         e = self.out_edges[stage]
         if self.backend == "p2p":
             t0 = time.monotonic()
-            try:
-                q = self.ctrl_out[stage].wait_grant(seq, self.timeout)
-            except Exception:
-                self._fail()
-                raise
+            ctrl = self.ctrl_out[stage]
+            q = self._wait_progressing(f"credit for sequence {seq} on {ctrl.name}",
+                                       lambda t: ctrl.wait_grant(seq, t))
             waited = time.monotonic() - t0
             if waited > 1e-4:
                 self.stats["credit_waits"] += 1
@@ -296,8 +313,10 @@ class StageBoundaries:
                 self._deadline_loop(f"a destination slot for batch {batch}",
                                     lambda: (self.progress(), key in self.grants)[1])
             p, ticket = self.grants.pop(key)
+            ctrl = self.ctrl_in[stage]
+            wire = self._wait_progressing(f"publication of sequence {seq} on {ctrl.name}",
+                                          lambda t: ctrl.wait_published(seq, t))
             try:
-                wire = self.ctrl_in[stage].wait_published(seq, self.timeout)
                 d = self.layout.match(wire, self.epoch, batch, seq, stage - 1)
             except Exception:
                 self._fail()
