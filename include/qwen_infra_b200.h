@@ -135,14 +135,15 @@ typedef struct QiKvView {
   int64_t data_page, data_row, data_head, sf_page, sf_row, sf_head;
 } QiKvView;
 
-/* k_out bf16 [Hkv, tokens, D]; vt_out bf16 [Hkv, D, vt_row] (vt_row % 64 == 0). */
+/* k_out f16 [Hkv, tokens, D]; vt_out f16 [Hkv, D, vt_row] (vt_row % 64 == 0); the
+ * values are the exact e2m1 x e4m3 products (global multipliers not applied). */
 int qi_kv_dequant(const QiKvView* kv, const int32_t* block_table, int tokens, void* k_out, void* vt_out,
                   int64_t vt_row, cudaStream_t stream);
 
 typedef struct QiAttention {
   const void* q;         /* bf16 [rows, Hq*D] (row stride q_row elements) */
-  const void* k;         /* bf16 [Hkv, kv_tokens, D] */
-  const void* vt;        /* bf16 [Hkv, D, vt_row] */
+  const void* k;         /* f16 [Hkv, kv_tokens, D] (from qi_kv_dequant) */
+  const void* vt;        /* f16 [Hkv, D, vt_row] */
   void* out;             /* bf16 [rows, Hq*D] (row stride out_row) */
   const float *k_global, *v_global;
   int* status;

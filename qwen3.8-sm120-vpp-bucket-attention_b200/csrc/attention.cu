@@ -1,18 +1,25 @@
-// Chunked causal GQA prefill attention on tcgen05 (sm_100a), bf16 operands,
-// fp32 accumulators in tensor memory and an fp32 online softmax.
+// Chunked causal GQA prefill attention on tcgen05 (sm_100a).
 //
-// Input K / V^T come from the paged NVFP4 cache through qi_kv_dequant (values
-// e2m1 * e4m3, exact in bf16); the fp32 global multipliers of K and V are
-// folded into the softmax scale and the output normalisation.
+// Operands: Q from the QK-norm/RoPE producer (bf16, converted to f16 in shared
+// memory - exact for normalised queries), K and V^T from qi_kv_dequant as f16
+// (e2m1 x e4m3 products are exact in f16); the fp32 global multipliers of K
+// and V are folded into the softmax scale and the output normalisation.  S and
+// O accumulate in fp32 in tensor memory; P = 2^(s*scale*log2e - m) is formed
+// with packed f16 exponentials and written back into the S columns of tensor
+// memory, from where the PV MMA reads it as its A operand (no shared-memory
+// round trip).
 //
-// One CTA = 128 query rows of one query head; 6 warps:
-//   warp 0     : TMA producer (Q once; K and V^T tiles of 128 keys, 2 stages),
-//   warp 1     : TMEM allocator + single MMA thread: S_j = Q K_j^T into one of
-//                two S buffers, O += P_{j-1} V_{j-1} (P from shared memory),
-//   warps 2..5 : softmax, one query row per thread (TMEM lane): online max /
-//                sum, O rescale in TMEM, P written to smem in the 128-byte
-//                swizzled K-major layout the MMA reads; final O / l epilogue.
-// S_{j+1} is computed by the tensor cores while the softmax works on S_j.
+// One CTA = 256 query rows (two 128-row tiles Q0, Q1) of one query head; 10 warps:
+//   warp 0      : TMA producer (Q once; K and V^T tiles of 128 keys, 2 stages),
+//   warp 1      : TMEM allocator + the single MMA-issuing thread,
+//   warps 2..5  : softmax of Q0 (one query row per thread = TMEM lane),
+//   warps 6..9  : softmax of Q1.
+// The MMA order per key tile j is S0_j, S1_j, PV0_j, PV1_j, so the tensor cores
+// run one tile's QK^T while the other tile's softmax runs (ping-pong).  The
+// running max is only moved (and O rescaled in TMEM) when it grows by more than
+// 2^8, which keeps rescales rare; P may then reach 256, well inside f16.
+#include <cuda_fp16.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -22,18 +29,18 @@ using namespace qi;
 
 namespace {
 
-constexpr int TQ = 128, TK = 128;
-constexpr int ATOM = 128 * 128;  // one 128-row x 128-byte swizzle column (16 KB)
-constexpr uint32_t S_COL0 = 0, S_COL1 = 128, O_COL = 256, TMEM_COLS = 512;
+constexpr int TQ = 128, TK = 128, NQ = 2;
+constexpr int ATOM = 128 * 128;            // one 128-row x 128-byte swizzle column (16 KB)
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 template <int HD>
 struct Geometry {
-  static constexpr int Q_BYTES = (HD / 64) * ATOM;  // HD/64 columns of [128 rows x 128 B]
-  static constexpr int K_BYTES = (HD / 64) * ATOM;
-  static constexpr int V_ATOM = HD * 128;  // one 64-key column of V^T: [HD rows x 128 B]
+  static constexpr int Q_TILE = (HD / 64) * ATOM;  // [128 rows x HD] 16-bit
+  static constexpr int K_BYTES = (HD / 64) * ATOM;  // [128 keys x HD]
+  static constexpr int V_ATOM = HD * 128;           // [HD rows x 64 keys]
   static constexpr int V_BYTES = 2 * V_ATOM;
-  static constexpr int P_BYTES = 2 * ATOM;
-  static constexpr int SMEM = Q_BYTES + 2 * K_BYTES + 2 * V_BYTES + P_BYTES + 1024 + 256;
+  static constexpr int SMEM = NQ * Q_TILE + 2 * K_BYTES + 2 * V_BYTES + 1024 + 256;
+  static constexpr uint32_t S_COL0 = 0, S_COL1 = 128, O_COL0 = 256, O_COL1 = 256 + HD;
 };
 
 struct AttnParams {
@@ -44,41 +51,87 @@ struct AttnParams {
   const float* v_global;
   float softmax_scale;
   int* status;
-  int q_tiles;
+  int q_blocks;
 };
 
+// kind::f16 with F16 A and B (format 0) and an fp32 accumulator.
+__host__ __device__ constexpr uint32_t idesc_f16(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+// D (+)= A . B with A read from tensor memory (lane = row, consecutive K pairs
+// packed in each 32-bit column) and B from shared memory.
+QI_DEV void mma_f16_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate), "r"(0u)
+      : "memory");
+}
+
+QI_DEV uint32_t pack_f16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+QI_DEV uint32_t ex2_f16x2(uint32_t x) {
+  uint32_t r;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(x));
+  return r;
+}
+QI_DEV float2 unpack_f16x2(uint32_t v) {
+  __half2 h = *reinterpret_cast<__half2*>(&v);
+  return __half22float2(h);
+}
+QI_DEV float ex2_f32(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+QI_DEV void tmem_st32u(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+      "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+      "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
 template <int HD>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     attn_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                 const __grid_constant__ CUtensorMap tv, AttnParams p) {
   using G = Geometry<HD>;
-  constexpr int Q_BYTES = G::Q_BYTES, K_BYTES = G::K_BYTES, V_BYTES = G::V_BYTES, P_BYTES = G::P_BYTES;
-  constexpr int V_ATOM = G::V_ATOM;
+  constexpr int Q_TILE = G::Q_TILE, K_BYTES = G::K_BYTES, V_BYTES = G::V_BYTES, V_ATOM = G::V_ATOM;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + Q_BYTES;
-  uint8_t* sV = sK + 2 * K_BYTES;
-  uint8_t* sP = sV + 2 * V_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + P_BYTES);
+  uint8_t* sQ = smem;              // NQ tiles
+  uint8_t* sK = sQ + NQ * Q_TILE;  // 2 stages
+  uint8_t* sV = sK + 2 * K_BYTES;  // 2 stages
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + 2 * V_BYTES);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2]
-  uint64_t* p_full = bars + 11;
-  uint64_t* o_done = bars + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* q_ready = bars + 1;
+  uint64_t* k_full = bars + 2;    // [2]
+  uint64_t* k_empty = bars + 4;   // [2]
+  uint64_t* v_full = bars + 6;    // [2]
+  uint64_t* v_empty = bars + 8;   // [2]
+  uint64_t* s_full = bars + 10;   // [NQ]
+  uint64_t* p_full = bars + 12;   // [NQ]
+  uint64_t* pv_done = bars + 14;  // [NQ]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bid = blockIdx.x;
-  const int qt = p.q_tiles - 1 - bid / p.qheads;  // heaviest (latest) query tiles first
+  const int qb = p.q_blocks - 1 - bid / p.qheads;  // heaviest (latest) query blocks first
   const int head = bid % p.qheads;
   const int kvh = head / p.group;
-  const int q0 = qt * TQ;
-  const int last_row = min(q0 + TQ, p.rows) - 1;
+  const int q0 = qb * (NQ * TQ);
+  const int last_row = min(q0 + NQ * TQ, p.rows) - 1;
   const int ntiles = (p.history + last_row + 1 + TK - 1) / TK;
 
   if (threadIdx.x == 0) {
@@ -86,19 +139,22 @@ __global__ void __launch_bounds__(192, 1)
     prefetch_tensormap(&tk);
     prefetch_tensormap(&tv);
     mbar_init(q_full, 1);
+    mbar_init(q_ready, NQ * 128);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
-      mbar_init(&s_full[i], 1);
     }
-    mbar_init(p_full, 128);
-    mbar_init(o_done, 1);
+    for (int i = 0; i < NQ; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&pv_done[i], 1);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -106,15 +162,19 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_expect_tx(q_full, Q_BYTES);
+      mbar_expect_tx(q_full, NQ * Q_TILE);
 #pragma unroll
-      for (int a = 0; a < HD / 64; ++a) tma_load_2d(sQ + a * ATOM, &tq, q_full, head * HD + 64 * a, q0);
+      for (int t = 0; t < NQ; ++t)
+#pragma unroll
+        for (int a = 0; a < HD / 64; ++a)
+          tma_load_2d(sQ + t * Q_TILE + a * ATOM, &tq, q_full, head * HD + 64 * a, q0 + t * TQ);
       for (int j = 0; j < ntiles; ++j) {
         const int s = j & 1;
         if (j >= 2 && !mbar_wait(&k_empty[s], ((j >> 1) - 1) & 1, abort_flag, p.status)) break;
         mbar_expect_tx(&k_full[s], K_BYTES);
 #pragma unroll
-        for (int a = 0; a < HD / 64; ++a) tma_load_3d(sK + s * K_BYTES + a * ATOM, &tk, &k_full[s], 64 * a, j * TK, kvh);
+        for (int a = 0; a < HD / 64; ++a)
+          tma_load_3d(sK + s * K_BYTES + a * ATOM, &tk, &k_full[s], 64 * a, j * TK, kvh);
         if (j >= 2 && !mbar_wait(&v_empty[s], ((j >> 1) - 1) & 1, abort_flag, p.status)) break;
         mbar_expect_tx(&v_full[s], V_BYTES);
         tma_load_3d(sV + s * V_BYTES, &tv, &v_full[s], j * TK, 0, kvh);
@@ -123,122 +183,146 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc_s = idesc_bf16(128), idesc_o = idesc_bf16(HD);
-      const uint32_t q_base = smem_u32(sQ), p_base = smem_u32(sP);
-      bool ok = mbar_wait(q_full, 0, abort_flag, p.status);
-      for (int j = 0; ok && j <= ntiles; ++j) {
-        if (j < ntiles) {
-          const int s = j & 1;
-          if (!(ok = mbar_wait(&k_full[s], (j >> 1) & 1, abort_flag, p.status))) break;
+      constexpr uint32_t idesc_s = idesc_f16(128), idesc_o = idesc_f16(HD);
+      const uint32_t q_base = smem_u32(sQ);
+      bool ok = mbar_wait(q_ready, 0, abort_flag, p.status);
+      tc_fence_after();
+      for (int j = 0; ok && j < ntiles; ++j) {
+        const int s = j & 1;
+        if (!(ok = mbar_wait(&k_full[s], (j >> 1) & 1, abort_flag, p.status))) break;
+        tc_fence_after();
+        const uint32_t k_base = smem_u32(sK + s * K_BYTES);
+#pragma unroll
+        for (int t = 0; t < NQ; ++t) {
+          // The S_t / P_t columns are free once PV_t of the previous key tile completed.
+          if (j >= 1 && !(ok = mbar_wait(&pv_done[t], (j - 1) & 1, abort_flag, p.status))) break;
           tc_fence_after();
-          const uint32_t k_base = smem_u32(sK + s * K_BYTES);
-          const uint32_t d_s = tmem + (s ? S_COL1 : S_COL0);
+          const uint32_t d_s = tmem + (t ? G::S_COL1 : G::S_COL0);
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
             const uint32_t off = (kk >> 2) * ATOM + (kk & 3) * 32;
-            mma_bf16(d_s, sdesc_kmajor_sw128(q_base + off), sdesc_kmajor_sw128(k_base + off), idesc_s, kk ? 1u : 0u);
+            mma_bf16(d_s, sdesc_kmajor_sw128(q_base + t * Q_TILE + off), sdesc_kmajor_sw128(k_base + off), idesc_s,
+                     kk ? 1u : 0u);
           }
-          tc_commit(&s_full[s]);
-          tc_commit(&k_empty[s]);
+          tc_commit(&s_full[t]);
         }
-        if (j >= 1) {
-          const int jp = j - 1, s = jp & 1;
-          if (!(ok = mbar_wait(p_full, jp & 1, abort_flag, p.status))) break;
-          if (!(ok = mbar_wait(&v_full[s], (jp >> 1) & 1, abort_flag, p.status))) break;
-          tc_fence_after();
-          const uint32_t v_base = smem_u32(sV + s * V_BYTES);
+        if (!ok) break;
+        tc_commit(&k_empty[s]);
+        if (!(ok = mbar_wait(&v_full[s], (j >> 1) & 1, abort_flag, p.status))) break;
+        tc_fence_after();
+        const uint32_t v_base = smem_u32(sV + s * V_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t poff = (kk >> 2) * ATOM + (kk & 3) * 32, voff = (kk >> 2) * V_ATOM + (kk & 3) * 32;
-            mma_bf16(tmem + O_COL, sdesc_kmajor_sw128(p_base + poff), sdesc_kmajor_sw128(v_base + voff), idesc_o,
-                     (jp | kk) ? 1u : 0u);
+        for (int t = 0; t < NQ; ++t) {
+          if (!(ok = mbar_wait(&p_full[t], j & 1, abort_flag, p.status))) break;
+          tc_fence_after();
+          const uint32_t a_p = tmem + (t ? G::S_COL1 : G::S_COL0), d_o = tmem + (t ? G::O_COL1 : G::O_COL0);
+#pragma unroll
+          for (int kk = 0; kk < TK / 16; ++kk) {
+            const uint32_t voff = (kk >> 2) * V_ATOM + (kk & 3) * 32;
+            mma_f16_ts(d_o, a_p + kk * 8, sdesc_kmajor_sw128(v_base + voff), idesc_o, (j | kk) ? 1u : 0u);
           }
-          tc_commit(o_done);
-          tc_commit(&v_empty[s]);
+          tc_commit(&pv_done[t]);
         }
+        if (!ok) break;
+        tc_commit(&v_empty[s]);
       }
     }
   } else {
-    const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;  // query row within the tile == TMEM lane
-    const int qpos = p.history + q0 + r;
+    const int t = (warp - 2) >> 2;      // query tile of this warpgroup
+    const int quarter = warp & 3;       // TMEM lane quarter
+    const int r = quarter * 32 + lane;  // row within the tile == TMEM lane
+    const int qrow = q0 + t * TQ + r;
+    const int qpos = p.history + qrow;
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+    const uint32_t s_addr = lane_base + (t ? G::S_COL1 : G::S_COL0);
+    const uint32_t o_addr = lane_base + (t ? G::O_COL1 : G::O_COL0);
+    // Convert this warpgroup's Q tile from bf16 to f16 in place (layout unchanged).
+    bool ok = mbar_wait(q_full, 0, abort_flag, p.status);
+    if (ok) {
+      uint4* q4 = reinterpret_cast<uint4*>(sQ + t * Q_TILE);
+      for (int i = (int)threadIdx.x - 64 - t * 128; i < Q_TILE / 16; i += 128) {
+        uint4 v = q4[i];
+        uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w[e]));
+          w[e] = pack_f16x2(f.x, f.y);
+        }
+        q4[i] = v;
+      }
+    }
+    fence_proxy_async_smem();
+    mbar_arrive(q_ready);
     const float scale2 = __fmul_rn(__fmul_rn(p.softmax_scale, *p.k_global), 1.4426950408889634f);
-    float m_run = -INFINITY, l_run = 0.0f;
-    bool ok = true;
-    uint8_t* prow = sP + r * 128;
-    for (int j = 0; j < ntiles; ++j) {
-      const int s = j & 1;
-      ok = mbar_wait(&s_full[s], (j >> 1) & 1, abort_flag, p.status);
+    float m_used = -INFINITY, l_run = 0.0f;
+    for (int j = 0; ok && j < ntiles; ++j) {
+      ok = mbar_wait(&s_full[t], j & 1, abort_flag, p.status);
       if (!ok) break;
       tc_fence_after();
       float sv[128];
       __syncwarp();
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(lane_base + (s ? S_COL1 : S_COL0) + c * 32, sv + c * 32);
+      for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + c * 32, sv + c * 32);
       const int kbase = j * TK;
       float mx = -INFINITY;
+      if (kbase + TK - 1 > qpos) {
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        const float x = (kbase + c <= qpos) ? sv[c] * scale2 : -INFINITY;
-        sv[c] = x;
-        mx = fmaxf(mx, x);
+        for (int c = 0; c < 128; ++c) {
+          if (kbase + c > qpos) sv[c] = -INFINITY;
+          mx = fmaxf(mx, sv[c]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) mx = fmaxf(mx, sv[c]);
       }
-      const float m_new = fmaxf(m_run, mx);
-      const float corr = (m_run == -INFINITY) ? 0.0f : exp2f(m_run - m_new);
+      const float m_tile = mx * scale2;
+      float corr = 1.0f;
+      bool rescale = false;
+      if (m_used == -INFINITY) {
+        m_used = m_tile;  // key 0 is visible to every row, so the first tile's max is finite
+      } else if (m_tile > m_used + kRescaleThreshold) {
+        corr = ex2_f32(m_used - m_tile);
+        m_used = m_tile;
+        rescale = true;
+      }
+      uint32_t pw[64];
       float sum = 0.0f;
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        const float e = (sv[c] == -INFINITY) ? 0.0f : exp2f(sv[c] - m_new);
-        sv[c] = e;
-        sum += e;
+      for (int c = 0; c < 64; ++c) {
+        const float d0 = fmaf(sv[2 * c], scale2, -m_used), d1 = fmaf(sv[2 * c + 1], scale2, -m_used);
+        pw[c] = ex2_f16x2(pack_f16x2(d0, d1));
+        const float2 e = unpack_f16x2(pw[c]);
+        sum += e.x + e.y;
       }
       l_run = l_run * corr + sum;
-      m_run = m_new;
-      if (j >= 1) {
-        // PV_{j-1} must be complete before O is rescaled and P overwritten.
-        ok = mbar_wait(o_done, (j - 1) & 1, abort_flag, p.status);
-        if (!ok) break;
-        tc_fence_after();
-        const bool need = __any_sync(0xffffffffu, corr != 1.0f);
-        if (need) {
+      // PV_t of the previous key tile has completed (the MMA thread waited for
+      // it before issuing this S_t), so O may be rescaled and P may replace S.
+      if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
-          for (int c = 0; c < HD / 32; ++c) {
-            float ov[32];
-            tmem_ld32(lane_base + O_COL + c * 32, ov);
+        for (int c = 0; c < HD / 32; ++c) {
+          float ov[32];
+          tmem_ld32(o_addr + c * 32, ov);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) ov[i] *= corr;
-            tmem_st32(lane_base + O_COL + c * 32, ov);
-          }
+          for (int i = 0; i < 32; ++i) ov[i] *= corr;
+          tmem_st32(o_addr + c * 32, ov);
         }
       }
-      // P row -> smem, 128-byte swizzle: 16-byte chunk c16 of row r lands at c16 ^ (r % 8).
-#pragma unroll
-      for (int ch = 0; ch < 16; ++ch) {
-        uint32_t w[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          __nv_bfloat162 h2 = __floats2bfloat162_rn(sv[ch * 8 + 2 * i], sv[ch * 8 + 2 * i + 1]);
-          w[i] = *reinterpret_cast<uint32_t*>(&h2);
-        }
-        const int atom = ch >> 3, c16 = ch & 7;
-        *reinterpret_cast<uint4*>(prow + atom * ATOM + ((c16 ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-      }
-      fence_proxy_async_smem();
+      tmem_st32u(s_addr, pw);
+      tmem_st32u(s_addr + 32, pw + 32);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[t]);
     }
-    if (ok) ok = mbar_wait(o_done, (ntiles - 1) & 1, abort_flag, p.status);
+    if (ok) ok = mbar_wait(&pv_done[t], (ntiles - 1) & 1, abort_flag, p.status);
     tc_fence_after();
     if (ok) {
       const float norm = __fdiv_rn(*p.v_global, l_run);
-      const int qrow = q0 + r;
       __nv_bfloat16* orow = p.out + (int64_t)qrow * p.out_row + (int64_t)head * HD;
 #pragma unroll 1
       for (int c = 0; c < HD / 32; ++c) {
         float ov[32];
         __syncwarp();
-        tmem_ld32(lane_base + O_COL + c * 32, ov);
+        tmem_ld32(o_addr + c * 32, ov);
         if (qrow < p.rows) {
           uint32_t w[16];
 #pragma unroll
@@ -257,7 +341,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, TMEM_COLS);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -278,17 +362,17 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// bf16 tensor with up to 3 dims; box {64 (128 B), box1, 1}, 128-byte swizzle.
-bool make_map_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
-                   uint32_t box1) {
+// 16-bit tensor with up to 3 dims; box {64 (128 B), box1, 1}, 128-byte swizzle.
+bool make_map16(CUtensorMap* map, CUtensorMapDataType type, const void* base, int rank, const uint64_t* dims,
+                const uint64_t* strides_bytes, uint32_t box1) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t d[3], s[2];
   cuuint32_t box[3] = {64, box1, 1}, estr[3] = {1, 1, 1};
   for (int i = 0; i < rank; ++i) d[i] = dims[i];
   for (int i = 0; i + 1 < rank; ++i) s[i] = strides_bytes[i];
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, s, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+  return fn(map, type, rank, const_cast<void*>(base), d, s, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -303,8 +387,9 @@ int launch_attention(const QiAttention* a, cudaStream_t stream) {
   const uint64_t ks[2] = {(uint64_t)HD * 2, (uint64_t)a->kv_tokens * HD * 2};
   const uint64_t vd[3] = {(uint64_t)a->kv_tokens, (uint64_t)HD, (uint64_t)a->kvheads};
   const uint64_t vs[2] = {(uint64_t)a->vt_row * 2, (uint64_t)a->vt_row * HD * 2};
-  if (!make_map_bf16(&mq, a->q, 2, qd, qs, 128) || !make_map_bf16(&mk, a->k, 3, kd, ks, 128) ||
-      !make_map_bf16(&mv, a->vt, 3, vd, vs, HD))
+  if (!make_map16(&mq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a->q, 2, qd, qs, 128) ||
+      !make_map16(&mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->k, 3, kd, ks, 128) ||
+      !make_map16(&mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->vt, 3, vd, vs, HD))
     return (int)cudaErrorInvalidValue;
   static bool configured[64] = {};
   int cur_dev = 0;
@@ -328,8 +413,8 @@ int launch_attention(const QiAttention* a, cudaStream_t stream) {
   p.v_global = a->v_global;
   p.softmax_scale = a->softmax_scale;
   p.status = a->status;
-  p.q_tiles = (a->rows + TQ - 1) / TQ;
-  attn_kernel<HD><<<p.q_tiles * a->qheads, 192, Geometry<HD>::SMEM, stream>>>(mq, mk, mv, p);
+  p.q_blocks = (a->rows + NQ * TQ - 1) / (NQ * TQ);
+  attn_kernel<HD><<<p.q_blocks * a->qheads, 320, Geometry<HD>::SMEM, stream>>>(mq, mk, mv, p);
   return (int)cudaPeekAtLastError();
 }
 

@@ -7,6 +7,8 @@
 //   * paged NVFP4 KV -> contiguous bf16 K and transposed V for attention.
 // Every fp32 step is an explicitly rounded IEEE operation; the reduction trees
 // are fixed, so the CPU restatement reproduces the quantised bytes exactly.
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 #include "qwen_infra_b200.h"
 
@@ -313,18 +315,19 @@ __global__ void fp8_rows_kernel(const float* __restrict__ w, int k, uint8_t* __r
   for (int c = threadIdx.x; c < k; c += blockDim.x) q[row * k + c] = (uint8_t)f_to_e4m3(__fdiv_rn(w[row * k + c], scale));
 }
 
-// Paged NVFP4 KV -> bf16 K [Hkv][tokens][D] and V^T [Hkv][D][v_stride].  The
-// stored values are e2m1 * e4m3 (exact in bf16); the fp32 global multiplier
-// is applied by the attention kernel.  One CTA per (64-token tile, head).
+// Paged NVFP4 KV -> f16 K [Hkv][tokens][D] and V^T [Hkv][D][v_stride].  The
+// stored values are e2m1 * e4m3 products (exact in f16: at most 5 significant
+// bits, magnitudes 2^-10 .. 2688); the fp32 global multiplier is applied by
+// the attention kernel.  One CTA per (64-token tile, head).
 template <int D>
 __global__ void __launch_bounds__(256) kv_dequant_kernel(const uint8_t* __restrict__ kc, const uint8_t* __restrict__ vc,
                                                          const uint8_t* __restrict__ ksf, const uint8_t* __restrict__ vsf,
                                                          const int32_t* __restrict__ block_table, int tokens, int page_size,
                                                          int64_t data_page, int64_t data_row, int64_t data_head,
                                                          int64_t sf_page, int64_t sf_row, int64_t sf_head,
-                                                         __nv_bfloat16* __restrict__ k_out, __nv_bfloat16* __restrict__ vt_out,
+                                                         __half* __restrict__ k_out, __half* __restrict__ vt_out,
                                                          int64_t k_head_stride, int64_t vt_head_stride, int64_t vt_row) {
-  __shared__ __nv_bfloat16 vtile[64][D + 8];
+  __shared__ __half vtile[64][D + 8];
   const int head = blockIdx.y;
   const int t0 = blockIdx.x * 64;
   const float lut[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
@@ -355,13 +358,13 @@ __global__ void __launch_bounds__(256) kv_dequant_kernel(const uint8_t* __restri
     }
     if (tok < tokens) {
       uint4 packed;
-      __nv_bfloat162* pk = reinterpret_cast<__nv_bfloat162*>(&packed);
+      __half2* pk = reinterpret_cast<__half2*>(&packed);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) pk[j] = __floats2bfloat162_rn(kv8[0][2 * j], kv8[0][2 * j + 1]);
+      for (int j = 0; j < 4; ++j) pk[j] = __floats2half2_rn(kv8[0][2 * j], kv8[0][2 * j + 1]);
       *reinterpret_cast<uint4*>(k_out + head * k_head_stride + (int64_t)tok * D + chunk * 8) = packed;
     }
 #pragma unroll
-    for (int j = 0; j < 8; ++j) vtile[tl][chunk * 8 + j] = __float2bfloat16_rn(kv8[1][j]);
+    for (int j = 0; j < 8; ++j) vtile[tl][chunk * 8 + j] = __float2half_rn(kv8[1][j]);
   }
   __syncthreads();
   // Write V^T rows: for each d, 64 consecutive tokens (128 bytes).
@@ -369,10 +372,10 @@ __global__ void __launch_bounds__(256) kv_dequant_kernel(const uint8_t* __restri
   for (int i = threadIdx.x; i < D * 32; i += blockDim.x) {
     const int d = i / 32, pair = i % 32;
     if (2 * pair < valid) {
-      __nv_bfloat162 v2;
+      __half2 v2;
       v2.x = vtile[2 * pair][d];
       v2.y = vtile[2 * pair + 1][d];
-      *reinterpret_cast<__nv_bfloat162*>(vt_out + head * vt_head_stride + (int64_t)d * vt_row + t0 + 2 * pair) = v2;
+      *reinterpret_cast<__half2*>(vt_out + head * vt_head_stride + (int64_t)d * vt_row + t0 + 2 * pair) = v2;
     }
   }
 }
@@ -592,7 +595,7 @@ int qi_kv_dequant(const QiKvView* kv, const int32_t* block_table, int tokens, vo
       static_cast<const uint8_t*>(kv->k_cache), static_cast<const uint8_t*>(kv->v_cache),                          \
       static_cast<const uint8_t*>(kv->k_scales), static_cast<const uint8_t*>(kv->v_scales), block_table, tokens,   \
       kv->page_size, kv->data_page, kv->data_row, kv->data_head, kv->sf_page, kv->sf_row, kv->sf_head,            \
-      static_cast<__nv_bfloat16*>(k_out), static_cast<__nv_bfloat16*>(vt_out), ks, vs, vt_row)
+      static_cast<__half*>(k_out), static_cast<__half*>(vt_out), ks, vs, vt_row)
   switch (kv->head_dim) {
     case 64: QI_KVD(64); break;
     case 128: QI_KVD(128); break;

@@ -251,15 +251,15 @@ def gemm_e4m3(a, b, *, m, n, k, row_scale=None, col_scale=None, alpha_value=1.0,
 
 
 def kv_dequant(kv, block_table, tokens, *, k_out=None, vt_out=None):
-    """Paged NVFP4 KV of one request -> bf16 K [Hkv, tokens, D] and V^T
-    [Hkv, D, vt_row] (vt_row = tokens rounded up to 64)."""
+    """Paged NVFP4 KV of one request -> f16 K [Hkv, tokens, D] and V^T
+    [Hkv, D, vt_row] (vt_row = tokens rounded up to 64), exact e2m1 x e4m3."""
     _cuda(block_table)
     vt_row = (tokens + 63) // 64 * 64
     d = kv.head_dim
     if k_out is None:
-        k_out = torch.empty((kv.kvheads, tokens, d), dtype=torch.bfloat16, device=kv.k.device)
+        k_out = torch.empty((kv.kvheads, tokens, d), dtype=torch.float16, device=kv.k.device)
     if vt_out is None:
-        vt_out = torch.empty((kv.kvheads, d, vt_row), dtype=torch.bfloat16, device=kv.k.device)
+        vt_out = torch.empty((kv.kvheads, d, vt_row), dtype=torch.float16, device=kv.k.device)
     view = kv.view()
     N.check(_run("kv_dequant", tokens * kv.kvheads * (d + d // 8 + 4 * d), "B", kv.k.device, lambda: N.lib().qi_kv_dequant(ct.byref(view), _ptr(block_table), tokens, _ptr(k_out), _ptr(vt_out), vt_row,
                                   _stream(kv.k.device))), "qi_kv_dequant")
@@ -269,7 +269,7 @@ def kv_dequant(kv, block_table, tokens, *, k_out=None, vt_out=None):
 def prefill_attention(q, k, vt, *, history, qheads, kvheads, head_dim, k_global, v_global, out=None,
                       softmax_scale=None, status=None, kv_tokens=None):
     """Causal GQA attention of ``rows`` queries at positions history.. over
-    keys 0 .. history+rows-1 held as bf16 K / V^T (from :func:`kv_dequant`)."""
+    keys 0 .. history+rows-1 held as f16 K / V^T (from :func:`kv_dequant`)."""
     _cuda(q, k, vt, k_global, v_global)
     rows = q.shape[0]
     if out is None:

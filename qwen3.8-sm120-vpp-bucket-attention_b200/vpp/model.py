@@ -166,8 +166,8 @@ class Workspace:
         self.act_q = torch.empty((max_rows, s.intermediate // 2), dtype=torch.uint8, **e)
         self.act_sf = torch.empty(K.scale_buffer_bytes(max_rows, s.intermediate), dtype=torch.uint8, **e)
         vt_row = (max_tokens + 63) // 64 * 64
-        self.kd = torch.empty(s.kvheads * max_tokens * d, dtype=torch.bfloat16, **e)
-        self.vt = torch.empty(s.kvheads * d * vt_row, dtype=torch.bfloat16, **e)
+        self.kd = torch.empty(s.kvheads * max_tokens * d, dtype=torch.float16, **e)
+        self.vt = torch.empty(s.kvheads * d * vt_row, dtype=torch.float16, **e)
         self.status = torch.zeros(1, dtype=torch.int32, **e)
         self.ping = [torch.empty((max_rows, h), dtype=torch.bfloat16, **e) for _ in range(4)]
 

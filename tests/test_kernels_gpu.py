@@ -283,11 +283,11 @@ def test_prefill_attention_matches_fp32(K, rows, history, qh, kvh, d):
     tokens = history + rows
     g = torch.Generator().manual_seed(81 + rows)
     q = (torch.randn(rows, qh * d, generator=g)).to(torch.bfloat16)
-    # K/V held as exact bf16 values; the global multipliers are folded in.
-    k = (torch.randn(kvh, tokens, d, generator=g) * 64).to(torch.bfloat16)
-    v = (torch.randn(kvh, tokens, d, generator=g) * 64).to(torch.bfloat16)
+    # K/V held as exact f16 values; the global multipliers are folded in.
+    k = (torch.randn(kvh, tokens, d, generator=g) * 64).to(torch.float16)
+    v = (torch.randn(kvh, tokens, d, generator=g) * 64).to(torch.float16)
     vt_row = (tokens + 63) // 64 * 64
-    vt = torch.zeros(kvh, d, vt_row, dtype=torch.bfloat16)
+    vt = torch.zeros(kvh, d, vt_row, dtype=torch.float16)
     vt[:, :, :tokens] = v.transpose(1, 2)
     kg, vg = 1.0 / 64, 1.0 / 64
     out = K.prefill_attention(q.to(DEV), k.to(DEV), vt.to(DEV), history=history, qheads=qh, kvheads=kvh,
