@@ -90,6 +90,27 @@ QI_DEV float ex2_f32(float x) {
   return r;
 }
 
+// 32 lanes x 32 columns load without the completion wait (callers issue several
+// and then one tcgen05.wait::ld).
+QI_DEV void tmem_ld32_nowait(uint32_t taddr, float* v) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+QI_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+QI_DEV uint32_t hadd2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
 QI_DEV void tmem_st32u(uint32_t taddr, const uint32_t* v) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
@@ -262,7 +283,8 @@ __global__ void __launch_bounds__(320, 1)
       float sv[128];
       __syncwarp();
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + c * 32, sv + c * 32);
+      for (int c = 0; c < 4; ++c) tmem_ld32_nowait(s_addr + c * 32, sv + c * 32);
+      tmem_wait_ld();
       const int kbase = j * TK;
       float mx = -INFINITY;
       if (kbase + TK - 1 > qpos) {
@@ -288,10 +310,15 @@ __global__ void __launch_bounds__(320, 1)
       uint32_t pw[64];
       float sum = 0.0f;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float d0 = fmaf(sv[2 * c], scale2, -m_used), d1 = fmaf(sv[2 * c + 1], scale2, -m_used);
-        pw[c] = ex2_f16x2(pack_f16x2(d0, d1));
-        const float2 e = unpack_f16x2(pw[c]);
+      for (int c0 = 0; c0 < 64; c0 += 4) {
+        // P for 8 keys; their sum is formed in f16 pairs (at most 8 * 256) and
+        // accumulated in fp32.
+#pragma unroll
+        for (int c = c0; c < c0 + 4; ++c) {
+          const float d0 = fmaf(sv[2 * c], scale2, -m_used), d1 = fmaf(sv[2 * c + 1], scale2, -m_used);
+          pw[c] = ex2_f16x2(pack_f16x2(d0, d1));
+        }
+        const float2 e = unpack_f16x2(hadd2(hadd2(pw[c0], pw[c0 + 1]), hadd2(pw[c0 + 2], pw[c0 + 3])));
         sum += e.x + e.y;
       }
       l_run = l_run * corr + sum;
