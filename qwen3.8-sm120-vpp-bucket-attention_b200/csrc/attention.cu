@@ -105,6 +105,23 @@ QI_DEV void tmem_ld32_nowait(uint32_t taddr, float* v) {
 }
 QI_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// 2^x on the FMA and integer pipes, for x <= 8 (P is rounded to f16 anyway):
+// n = rint(x) via the 1.5*2^23 rounding constant, f = x - n in [-1/2, 1/2],
+// 2^f by a degree-3 polynomial (weighted least-squares fit of 2^f on
+// [-1/2, 1/2] at Chebyshev nodes; relative error 1.2e-4, under the f16
+// rounding of P), exponent added as n << 23.
+// Offloads part of the exponentials from the 16-per-clock MUFU unit.
+QI_DEV float ex2_poly(float x) {
+  x = fmaxf(x, -127.0f);
+  const float t = __fadd_rn(x, 12582912.0f);
+  const float n = __fsub_rn(t, 12582912.0f);
+  const float f = __fsub_rn(x, n);
+  float p = fmaf(f, 0x1.c5fb94p-5f, 0x1.f00c82p-3f);
+  p = fmaf(p, f, 0x1.62eb0cp-1f);
+  p = fmaf(p, f, 1.0f);
+  return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
+}
+
 QI_DEV uint32_t hadd2(uint32_t a, uint32_t b) {
   uint32_t r;
   asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
@@ -308,19 +325,23 @@ __global__ void __launch_bounds__(320, 1)
         rescale = true;
       }
       uint32_t pw[64];
-      float sum = 0.0f;
+      float sum0 = 0.0f, sum1 = 0.0f;
 #pragma unroll
-      for (int c0 = 0; c0 < 64; c0 += 4) {
-        // P for 8 keys; their sum is formed in f16 pairs (at most 8 * 256) and
-        // accumulated in fp32.
-#pragma unroll
-        for (int c = c0; c < c0 + 4; ++c) {
-          const float d0 = fmaf(sv[2 * c], scale2, -m_used), d1 = fmaf(sv[2 * c + 1], scale2, -m_used);
-          pw[c] = ex2_f16x2(pack_f16x2(d0, d1));
+      for (int c = 0; c < 64; ++c) {
+        const float d0 = fmaf(sv[2 * c], scale2, -m_used), d1 = fmaf(sv[2 * c + 1], scale2, -m_used);
+        float e0, e1;
+        if ((c & 3) == 3) {  // one pair in four on the FMA pipe, the rest on MUFU
+          e0 = ex2_poly(d0);
+          e1 = ex2_poly(d1);
+        } else {
+          e0 = ex2_f32(d0);
+          e1 = ex2_f32(d1);
         }
-        const float2 e = unpack_f16x2(hadd2(hadd2(pw[c0], pw[c0 + 1]), hadd2(pw[c0 + 2], pw[c0 + 3])));
-        sum += e.x + e.y;
+        sum0 += e0;
+        sum1 += e1;
+        pw[c] = pack_f16x2(e0, e1);
       }
+      const float sum = sum0 + sum1;
       l_run = l_run * corr + sum;
       // PV_t of the previous key tile has completed (the MMA thread waited for
       // it before issuing this S_t), so O may be rescaled and P may replace S.
