@@ -136,17 +136,24 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (!(ok = mbar_wait(&full[s], (it / STAGES) & 1, abort_flag, p.status))) break;
           tc_fence_after();
           const uint32_t a_base = smem_u32(sA + s * A_BYTES), b_base = smem_u32(sB + s * B_BYTES);
+          if constexpr (kFp4) {
+            // All of this stage's scale factors first, then its four MMAs.
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint32_t sfa_t = tmem + SFA_COL + s * 16 + kk * 4, sfb_t = tmem + SFB_COL + s * 32 + kk * 8;
+              tc_cp_sf(sfa_t, sdesc_sf_atom(smem_u32(sSFA + s * SFA_BYTES + kk * 512)));
+              tc_cp_sf(sfb_t, sdesc_sf_atom(smem_u32(sSFB + s * SFB_BYTES + kk * 512)));
+              tc_cp_sf(sfb_t + 4, sdesc_sf_atom(smem_u32(sSFB + s * SFB_BYTES + 2048 + kk * 512)));
+            }
+          }
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t adesc = sdesc_kmajor_sw128(a_base + kk * 32);
             const uint64_t bdesc = sdesc_kmajor_sw128(b_base + kk * 32);
             const uint32_t acc = (kt | kk) ? 1u : 0u;
             if constexpr (kFp4) {
-              const uint32_t sfa_t = tmem + SFA_COL + s * 16 + kk * 4, sfb_t = tmem + SFB_COL + s * 32 + kk * 8;
-              tc_cp_sf(sfa_t, sdesc_sf_atom(smem_u32(sSFA + s * SFA_BYTES + kk * 512)));
-              tc_cp_sf(sfb_t, sdesc_sf_atom(smem_u32(sSFB + s * SFB_BYTES + kk * 512)));
-              tc_cp_sf(sfb_t + 4, sdesc_sf_atom(smem_u32(sSFB + s * SFB_BYTES + 2048 + kk * 512)));
-              mma_nvfp4(tmem + ACC_COL, adesc, bdesc, idesc, sfa_t, sfb_t, acc);
+              mma_nvfp4(tmem + ACC_COL, adesc, bdesc, idesc, tmem + SFA_COL + s * 16 + kk * 4,
+                        tmem + SFB_COL + s * 32 + kk * 8, acc);
             } else {
               mma_f8(tmem + ACC_COL, adesc, bdesc, idesc, acc);
             }
