@@ -122,6 +122,44 @@ QI_DEV float ex2_poly(float x) {
   return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
 }
 
+// Packed fp32 pair arithmetic (one instruction for two lanes' worth of work).
+QI_DEV float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+QI_DEV float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+QI_DEV float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// ex2_poly on a pair with packed arithmetic.
+QI_DEV float2 ex2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -127.0f);
+  x.y = fmaxf(x.y, -127.0f);
+  const float2 t = fadd2(x, make_float2(12582912.0f, 12582912.0f));
+  const float2 n = fadd2(t, make_float2(-12582912.0f, -12582912.0f));
+  const float2 f = ffma2(n, make_float2(-1.0f, -1.0f), x);
+  float2 p = ffma2(f, make_float2(0x1.c5fb94p-5f, 0x1.c5fb94p-5f), make_float2(0x1.f00c82p-3f, 0x1.f00c82p-3f));
+  p = ffma2(p, f, make_float2(0x1.62eb0cp-1f, 0x1.62eb0cp-1f));
+  p = ffma2(p, f, make_float2(1.0f, 1.0f));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
 QI_DEV uint32_t hadd2(uint32_t a, uint32_t b) {
   uint32_t r;
   asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
@@ -297,22 +335,26 @@ __global__ void __launch_bounds__(320, 1)
       ok = mbar_wait(&s_full[t], j & 1, abort_flag, p.status);
       if (!ok) break;
       tc_fence_after();
-      float sv[128];
-      __syncwarp();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32_nowait(s_addr + c * 32, sv + c * 32);
-      tmem_wait_ld();
+      // Two passes over S in TMEM (64 columns at a time) keep the live
+      // registers low: pass 1 finds the row max, pass 2 forms P = 2^(s*scale2 - m)
+      // and writes it back as f16 pairs over the columns just read.
       const int kbase = j * TK;
+      const bool diagonal = kbase + TK - 1 > qpos;
       float mx = -INFINITY;
-      if (kbase + TK - 1 > qpos) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          if (kbase + c > qpos) sv[c] = -INFINITY;
-          mx = fmaxf(mx, sv[c]);
+      for (int h = 0; h < 2; ++h) {
+        float sv[64];
+        __syncwarp();
+        tmem_ld32_nowait(s_addr + h * 64, sv);
+        tmem_ld32_nowait(s_addr + h * 64 + 32, sv + 32);
+        tmem_wait_ld();
+        if (diagonal) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (kbase + h * 64 + c > qpos) sv[c] = -INFINITY;
         }
-      } else {
 #pragma unroll
-        for (int c = 0; c < 128; ++c) mx = fmaxf(mx, sv[c]);
+        for (int c = 0; c < 64; c += 2) mx = fmax3(mx, sv[c], sv[c + 1]);
       }
       const float m_tile = mx * scale2;
       float corr = 1.0f;
@@ -324,24 +366,38 @@ __global__ void __launch_bounds__(320, 1)
         m_used = m_tile;
         rescale = true;
       }
-      uint32_t pw[64];
-      float sum0 = 0.0f, sum1 = 0.0f;
+      const float2 sc2 = make_float2(scale2, scale2), nm2 = make_float2(-m_used, -m_used);
+      float2 acc = make_float2(0.0f, 0.0f);
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float d0 = fmaf(sv[2 * c], scale2, -m_used), d1 = fmaf(sv[2 * c + 1], scale2, -m_used);
-        float e0, e1;
-        if ((c & 3) == 3) {  // one pair in four on the FMA pipe, the rest on MUFU
-          e0 = ex2_poly(d0);
-          e1 = ex2_poly(d1);
-        } else {
-          e0 = ex2_f32(d0);
-          e1 = ex2_f32(d1);
+      for (int h = 0; h < 2; ++h) {
+        float sv[64];
+        uint32_t pw[32];
+        __syncwarp();
+        tmem_ld32_nowait(s_addr + h * 64, sv);
+        tmem_ld32_nowait(s_addr + h * 64 + 32, sv + 32);
+        tmem_wait_ld();
+        if (diagonal) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (kbase + h * 64 + c > qpos) sv[c] = -INFINITY;
         }
-        sum0 += e0;
-        sum1 += e1;
-        pw[c] = pack_f16x2(e0, e1);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float2 d = ffma2(make_float2(sv[2 * c], sv[2 * c + 1]), sc2, nm2);
+          float2 e;
+          if ((c & 3) == 3) {  // one pair in four on the FMA pipe, the rest on MUFU
+            e = ex2_poly2(d);
+          } else {
+            e = make_float2(ex2_f32(d.x), ex2_f32(d.y));
+          }
+          acc = fadd2(acc, e);
+          pw[c] = pack_f16x2(e.x, e.y);
+        }
+        // P for keys [64h, 64h+64) -> S columns [32h, 32h+32); pass 2 of the
+        // second half reads columns 64..127, which this store does not touch.
+        tmem_st32u(s_addr + h * 32, pw);
       }
-      const float sum = sum0 + sum1;
+      const float sum = acc.x + acc.y;
       l_run = l_run * corr + sum;
       // PV_t of the previous key tile has completed (the MMA thread waited for
       // it before issuing this S_t), so O may be rescaled and P may replace S.
@@ -355,8 +411,6 @@ __global__ void __launch_bounds__(320, 1)
           tmem_st32(o_addr + c * 32, ov);
         }
       }
-      tmem_st32u(s_addr, pw);
-      tmem_st32u(s_addr + 32, pw + 32);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       mbar_arrive(&p_full[t]);
