@@ -81,9 +81,6 @@ class FoldedRank:
         for batch, stage in self.order:
             ch = self.chunks[batch]
             ctx = ctxs[batch]
-            if record_events:
-                ev0 = torch.cuda.Event(enable_timing=True)
-                ev0.record(stream)
             if stage == 0:
                 if host_embeds is not None:
                     hidden = host_embeds[ch.request][ch.start:ch.start + ch.rows].to(self.device, non_blocking=True)
@@ -94,6 +91,9 @@ class FoldedRank:
                 hidden, residual = self.fold[0][:ch.rows], self.fold[1][:ch.rows]
             else:
                 hidden, residual = self.transport.receive(batch, stage, ch.rows)
+            if record_events:  # after the input is ready: stage time excludes waiting
+                ev0 = torch.cuda.Event(enable_timing=True)
+                ev0.record(stream)
             span = L.stage_layers(stage, G, self.shape.layers)
             on_residual = None
             if stage == G - 1:
