@@ -14,8 +14,8 @@
 //   warp 1      : TMEM allocator + the single MMA-issuing thread,
 //   warps 2..5  : softmax of Q0 (one query row per thread = TMEM lane),
 //   warps 6..9  : softmax of Q1.
-// The MMA order per key tile j is S0_j, S1_j, PV0_j, PV1_j, so the tensor cores
-// run one tile's QK^T while the other tile's softmax runs (ping-pong).  The
+// The MMA order is PV0_j, S0_{j+1}, PV1_j, S1_{j+1}, so the tensor cores run
+// one tile's PV and next QK^T while the other tile's softmax runs (ping-pong).  The
 // running max is only moved (and O rescaled in TMEM) when it grows by more than
 // 2^8, which keeps rescales rare; P may then reach 256, well inside f16.
 #include <cuda_fp16.h>
@@ -259,48 +259,64 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
+      // Issue order: S0_0 S1_0 | PV0_0 S0_1 PV1_0 S1_1 | PV0_1 S0_2 ... so that
+      // the softmax of one tile overlaps the other tile's PV + S pair.  S_t(j+1)
+      // overwrites the TMEM columns that PV_t(j), issued just before it by this
+      // thread, reads P_t(j) from; tcgen05.mma operations issued by one thread
+      // execute in order, so the read precedes the overwrite.  The commit that
+      // signals S_t(j+1) covers PV_t(j) as well, so the softmax may rescale O
+      // once it sees S_t(j+1).
       constexpr uint32_t idesc_s = idesc_f16(128), idesc_o = idesc_f16(HD);
       const uint32_t q_base = smem_u32(sQ);
       bool ok = mbar_wait(q_ready, 0, abort_flag, p.status);
       tc_fence_after();
+      auto issue_s = [&](int t, int j) {
+        const uint32_t k_base = smem_u32(sK + (j & 1) * K_BYTES);
+        const uint32_t d_s = tmem + (t ? G::S_COL1 : G::S_COL0);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * ATOM + (kk & 3) * 32;
+          mma_bf16(d_s, sdesc_kmajor_sw128(q_base + t * Q_TILE + off), sdesc_kmajor_sw128(k_base + off), idesc_s,
+                   kk ? 1u : 0u);
+        }
+        tc_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t v_base = smem_u32(sV + (j & 1) * V_BYTES);
+        const uint32_t a_p = tmem + (t ? G::S_COL1 : G::S_COL0), d_o = tmem + (t ? G::O_COL1 : G::O_COL0);
+#pragma unroll
+        for (int kk = 0; kk < TK / 16; ++kk) {
+          const uint32_t voff = (kk >> 2) * V_ATOM + (kk & 3) * 32;
+          mma_f16_ts(d_o, a_p + kk * 8, sdesc_kmajor_sw128(v_base + voff), idesc_o, (j | kk) ? 1u : 0u);
+        }
+      };
+      if (ok && (ok = mbar_wait(&k_full[0], 0, abort_flag, p.status))) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+        tc_commit(&k_empty[0]);
+      }
       for (int j = 0; ok && j < ntiles; ++j) {
         const int s = j & 1;
-        if (!(ok = mbar_wait(&k_full[s], (j >> 1) & 1, abort_flag, p.status))) break;
-        tc_fence_after();
-        const uint32_t k_base = smem_u32(sK + s * K_BYTES);
-#pragma unroll
-        for (int t = 0; t < NQ; ++t) {
-          // The S_t / P_t columns are free once PV_t of the previous key tile completed.
-          if (j >= 1 && !(ok = mbar_wait(&pv_done[t], (j - 1) & 1, abort_flag, p.status))) break;
-          tc_fence_after();
-          const uint32_t d_s = tmem + (t ? G::S_COL1 : G::S_COL0);
-#pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * ATOM + (kk & 3) * 32;
-            mma_bf16(d_s, sdesc_kmajor_sw128(q_base + t * Q_TILE + off), sdesc_kmajor_sw128(k_base + off), idesc_s,
-                     kk ? 1u : 0u);
-          }
-          tc_commit(&s_full[t]);
-        }
-        if (!ok) break;
-        tc_commit(&k_empty[s]);
+        const bool more = j + 1 < ntiles;
         if (!(ok = mbar_wait(&v_full[s], (j >> 1) & 1, abort_flag, p.status))) break;
+        if (more && !(ok = mbar_wait(&k_full[s ^ 1], ((j + 1) >> 1) & 1, abort_flag, p.status))) break;
+        if (!(ok = mbar_wait(&p_full[0], j & 1, abort_flag, p.status))) break;
         tc_fence_after();
-        const uint32_t v_base = smem_u32(sV + s * V_BYTES);
-#pragma unroll
-        for (int t = 0; t < NQ; ++t) {
-          if (!(ok = mbar_wait(&p_full[t], j & 1, abort_flag, p.status))) break;
-          tc_fence_after();
-          const uint32_t a_p = tmem + (t ? G::S_COL1 : G::S_COL0), d_o = tmem + (t ? G::O_COL1 : G::O_COL0);
-#pragma unroll
-          for (int kk = 0; kk < TK / 16; ++kk) {
-            const uint32_t voff = (kk >> 2) * V_ATOM + (kk & 3) * 32;
-            mma_f16_ts(d_o, a_p + kk * 8, sdesc_kmajor_sw128(v_base + voff), idesc_o, (j | kk) ? 1u : 0u);
-          }
-          tc_commit(&pv_done[t]);
-        }
-        if (!ok) break;
+        issue_pv(0, j);
+        if (more) issue_s(0, j + 1);
+        if (!(ok = mbar_wait(&p_full[1], j & 1, abort_flag, p.status))) break;
+        tc_fence_after();
+        issue_pv(1, j);
         tc_commit(&v_empty[s]);
+        if (more) {
+          issue_s(1, j + 1);
+          tc_commit(&k_empty[s ^ 1]);
+        }
+      }
+      if (ok) {
+        tc_commit(&pv_done[0]);
+        tc_commit(&pv_done[1]);
       }
     }
   } else {
@@ -399,8 +415,8 @@ __global__ void __launch_bounds__(320, 1)
       }
       const float sum = acc.x + acc.y;
       l_run = l_run * corr + sum;
-      // PV_t of the previous key tile has completed (the MMA thread waited for
-      // it before issuing this S_t), so O may be rescaled and P may replace S.
+      // PV_t of the previous key tile has completed (the commit that signalled
+      // this S_t covers it), so O may be rescaled.
       if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
         for (int c = 0; c < HD / 32; ++c) {
@@ -415,7 +431,7 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_before();
       mbar_arrive(&p_full[t]);
     }
-    if (ok) ok = mbar_wait(&pv_done[t], (ntiles - 1) & 1, abort_flag, p.status);
+    if (ok) ok = mbar_wait(&pv_done[t], 0, abort_flag, p.status);
     tc_fence_after();
     if (ok) {
       const float norm = __fdiv_rn(*p.v_global, l_run);
