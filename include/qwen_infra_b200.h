@@ -150,16 +150,28 @@ typedef struct QiAttention {
   int rows, history, kv_tokens, qheads, kvheads, head_dim;
   int64_t q_row, out_row, vt_row;
   float softmax_scale;
+  /* Optional key-range split workspace (256-byte aligned, zero-filled before
+   * its first use; the kernel leaves its counters consistent, so it is reused
+   * as is).  With it, the units of the last, partly idle wave of CTAs are
+   * split into two key-range halves that combine in the kernel; NULL or too
+   * small: no split.  Calls that overlap on the GPU need separate workspaces. */
+  void* workspace;
+  int64_t workspace_bytes;
 } QiAttention;
 
 int qi_prefill_attention(const QiAttention* p, cudaStream_t stream);
+
+/* Bytes of QiAttention.workspace that allow every split the current device's
+ * SM count can ask for at this head_dim. */
+int qi_prefill_attention_workspace_bytes(int head_dim, int64_t* bytes);
 
 /* qi_kv_dequant + qi_prefill_attention in one call that allocates nothing, for
  * callers that cannot allocate device memory (inside a graph capture or an
  * allocator callback, or a plugin host that only hands out input and output
  * buffers).  No counterpart in the reference project.  The f16 K / V^T scratch
- * lives in a 32 MiB static device array that every GPU loading this library
- * holds until exit; history + rows is limited to what fits (Hkv * D * 4 bytes
+ * lives in a 32 MiB static device array (and the attention split workspace in
+ * a second one of about 21 MB) that every GPU loading this library holds until
+ * exit; history + rows is limited to what fits (Hkv * D * 4 bytes
  * per token, plus V^T padding to 64 tokens: 8192 tokens for 8 KV heads of 128),
  * larger calls return cudaErrorInvalidValue.  All calls share the array:
  * calls that overlap on the GPU race, so order them on one stream.  The first

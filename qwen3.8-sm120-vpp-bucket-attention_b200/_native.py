@@ -67,7 +67,7 @@ class QiAttention(ct.Structure):
         [(n, _vp) for n in ("q", "k", "vt", "out", "k_global", "v_global", "status")]
         + [(n, _i32) for n in ("rows", "history", "kv_tokens", "qheads", "kvheads", "head_dim")]
         + [(n, _i64) for n in ("q_row", "out_row", "vt_row")]
-        + [("softmax_scale", _f32)]
+        + [("softmax_scale", _f32), ("workspace", _vp), ("workspace_bytes", _i64)]
     )
 
 
@@ -85,6 +85,7 @@ EXPORTS = {
     "qi_gemm_resources": ([ct.POINTER(_i32)], _i32),
     "qi_kv_dequant": ([ct.POINTER(QiKvView), _vp, _i32, _vp, _vp, _i64, _vp], _i32),
     "qi_prefill_attention": ([ct.POINTER(QiAttention), _vp], _i32),
+    "qi_prefill_attention_workspace_bytes": ([_i32, ct.POINTER(_i64)], _i32),
     "qi_nvfp4_quantize": ([_vp, _i64, _i32, _vp, _vp, _vp, _vp], _i32),
     "qi_fp8_quantize_rows": ([_vp, _i32, _i32, _vp, _vp, _vp], _i32),
     "qi_abi_struct_sizes": ([ct.POINTER(_i32)], _i32),

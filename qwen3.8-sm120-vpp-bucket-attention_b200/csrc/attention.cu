@@ -52,7 +52,26 @@ struct AttnParams {
   float softmax_scale;
   int* status;
   int q_blocks;
+  // Key-range split of the lightest units (see split_plan): CTAs with
+  // blockIdx >= split_first each take half of the key tiles of one unit and
+  // combine through the workspace.
+  int split_first;
+  unsigned* ws_count;  // [slots] arrival counters (parity = which piece is last)
+  float* ws_ml;        // [slots][2][NQ*TQ][2] (m, l) per row and piece
+  float* ws_o;         // [slots][2][NQ*TQ][HD] unnormalised O per row and piece
 };
+
+// Workspace of the key-range split for `slots` split units of head_dim hd.
+// The arrival counters persist across launches, so they sit at a fixed place
+// (the first 4 KB, up to 1024 slots) whatever a launch's split count; the
+// (m, l) and O halves after them are rewritten by every launch that reads them.
+constexpr int kMaxSlots = 1024;
+__host__ __device__ constexpr int64_t ws_count_bytes(int) { return (int64_t)kMaxSlots * 4; }
+__host__ __device__ constexpr int64_t ws_ml_bytes(int slots) { return (int64_t)slots * 2 * NQ * TQ * 2 * 4; }
+__host__ __device__ constexpr int64_t ws_o_bytes(int slots, int hd) { return (int64_t)slots * 2 * NQ * TQ * hd * 4; }
+__host__ __device__ constexpr int64_t ws_bytes(int slots, int hd) {
+  return ws_count_bytes(slots) + ws_ml_bytes(slots) + ws_o_bytes(slots, hd);
+}
 
 // kind::f16 with F16 A and B (format 0) and an fp32 accumulator.
 __host__ __device__ constexpr uint32_t idesc_f16(int n) {
@@ -177,6 +196,29 @@ QI_DEV void tmem_st32u(uint32_t taddr, const uint32_t* v) {
       : "memory");
 }
 
+QI_DEV void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// 32 output columns of one row as bf16: a * norm, or (a*wa + b*wb) * norm
+// when a second half b is given (lower-key half first).
+QI_DEV void store_out_row(__nv_bfloat16* dst, const float* a, float norm, const float* b, float wa, float wb) {
+  uint32_t w[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    float x0 = a[2 * i], x1 = a[2 * i + 1];
+    if (b) {
+      x0 = __fadd_rn(__fmul_rn(x0, wa), __fmul_rn(b[2 * i], wb));
+      x1 = __fadd_rn(__fmul_rn(x1, wa), __fmul_rn(b[2 * i + 1], wb));
+    }
+    __nv_bfloat162 h2 = __floats2bfloat162_rn(x0 * norm, x1 * norm);
+    w[i] = *reinterpret_cast<uint32_t*>(&h2);
+  }
+  uint4* o = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+}
+
 template <int HD>
 __global__ void __launch_bounds__(320, 1)
     attn_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -203,12 +245,19 @@ __global__ void __launch_bounds__(320, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bid = blockIdx.x;
-  const int qb = p.q_blocks - 1 - bid / p.qheads;  // heaviest (latest) query blocks first
-  const int head = bid % p.qheads;
+  // Unit = (query block, head); units run heaviest (latest query block) first.
+  // CTAs from split_first on take one half of the key tiles of a split unit.
+  const int slot = bid < p.split_first ? -1 : (bid - p.split_first) >> 1;
+  const int piece = bid < p.split_first ? -1 : (bid - p.split_first) & 1;
+  const int unit = bid < p.split_first ? bid : p.split_first + slot;
+  const int qb = p.q_blocks - 1 - unit / p.qheads;
+  const int head = unit % p.qheads;
   const int kvh = head / p.group;
   const int q0 = qb * (NQ * TQ);
   const int last_row = min(q0 + NQ * TQ, p.rows) - 1;
-  const int ntiles = (p.history + last_row + 1 + TK - 1) / TK;
+  const int unit_tiles = (p.history + last_row + 1 + TK - 1) / TK;
+  const int j_first = piece == 1 ? unit_tiles / 2 : 0;  // first key tile of this CTA
+  const int ntiles = piece == 0 ? unit_tiles / 2 : unit_tiles - j_first;
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&tq);
@@ -250,11 +299,11 @@ __global__ void __launch_bounds__(320, 1)
         mbar_expect_tx(&k_full[s], K_BYTES);
 #pragma unroll
         for (int a = 0; a < HD / 64; ++a)
-          tma_load_3d(sK + s * K_BYTES + a * ATOM, &tk, &k_full[s], 64 * a, j * TK, kvh);
+          tma_load_3d(sK + s * K_BYTES + a * ATOM, &tk, &k_full[s], 64 * a, (j_first + j) * TK, kvh);
         if (j >= 2 && !mbar_wait(&v_empty[s], ((j >> 1) - 1) & 1, abort_flag, p.status)) break;
         mbar_expect_tx(&v_full[s], V_BYTES);
-        tma_load_3d(sV + s * V_BYTES, &tv, &v_full[s], j * TK, 0, kvh);
-        tma_load_3d(sV + s * V_BYTES + V_ATOM, &tv, &v_full[s], j * TK + 64, 0, kvh);
+        tma_load_3d(sV + s * V_BYTES, &tv, &v_full[s], (j_first + j) * TK, 0, kvh);
+        tma_load_3d(sV + s * V_BYTES + V_ATOM, &tv, &v_full[s], (j_first + j) * TK + 64, 0, kvh);
       }
     }
   } else if (warp == 1) {
@@ -354,7 +403,7 @@ __global__ void __launch_bounds__(320, 1)
       // Two passes over S in TMEM (64 columns at a time) keep the live
       // registers low: pass 1 finds the row max, pass 2 forms P = 2^(s*scale2 - m)
       // and writes it back as f16 pairs over the columns just read.
-      const int kbase = j * TK;
+      const int kbase = (j_first + j) * TK;
       const bool diagonal = kbase + TK - 1 > qpos;
       float mx = -INFINITY;
 #pragma unroll
@@ -376,13 +425,17 @@ __global__ void __launch_bounds__(320, 1)
       float corr = 1.0f;
       bool rescale = false;
       if (m_used == -INFINITY) {
-        m_used = m_tile;  // key 0 is visible to every row, so the first tile's max is finite
+        // First tile with a visible key for this row (key 0 is visible to every
+        // row; in the upper half of a split unit a row may see no key at all
+        // for a while, and then m_used stays -inf and P stays 0).
+        m_used = m_tile;
       } else if (m_tile > m_used + kRescaleThreshold) {
         corr = ex2_f32(m_used - m_tile);
         m_used = m_tile;
         rescale = true;
       }
-      const float2 sc2 = make_float2(scale2, scale2), nm2 = make_float2(-m_used, -m_used);
+      const float m_sub = m_used == -INFINITY ? 0.0f : m_used;
+      const float2 sc2 = make_float2(scale2, scale2), nm2 = make_float2(-m_sub, -m_sub);
       float2 acc = make_float2(0.0f, 0.0f);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
@@ -433,24 +486,76 @@ __global__ void __launch_bounds__(320, 1)
     }
     if (ok) ok = mbar_wait(&pv_done[t], 0, abort_flag, p.status);
     tc_fence_after();
-    if (ok) {
-      const float norm = __fdiv_rn(*p.v_global, l_run);
-      __nv_bfloat16* orow = p.out + (int64_t)qrow * p.out_row + (int64_t)head * HD;
+    const int prow = t * TQ + r;  // row within the unit
+    __nv_bfloat16* orow = p.out + (int64_t)qrow * p.out_row + (int64_t)head * HD;
+    if (piece < 0) {
+      if (ok) {
+        const float norm = __fdiv_rn(*p.v_global, l_run);
 #pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
-        float ov[32];
-        __syncwarp();
-        tmem_ld32(o_addr + c * 32, ov);
-        if (qrow < p.rows) {
-          uint32_t w[16];
+        for (int c = 0; c < HD / 32; ++c) {
+          float ov[32];
+          __syncwarp();
+          tmem_ld32(o_addr + c * 32, ov);
+          if (qrow < p.rows) store_out_row(orow + c * 32, ov, norm, nullptr, 0.0f, 0.0f);
+        }
+      }
+    } else {
+      // Split unit: publish this half's (m, l, O), then the CTA that arrives
+      // second combines both halves (its own from TMEM, the other's from the
+      // workspace).  No CTA waits for another.  Both pieces always arrive,
+      // so the counter's parity stays right even after an aborted launch.
+      float* my_o = p.ws_o + ((int64_t)(slot * 2 + piece) * NQ * TQ + prow) * HD;
+      float* my_ml = p.ws_ml + ((int64_t)(slot * 2 + piece) * NQ * TQ + prow) * 2;
+      if (ok) {
+#pragma unroll 1
+        for (int c = 0; c < HD / 32; ++c) {
+          float ov[32];
+          __syncwarp();
+          tmem_ld32(o_addr + c * 32, ov);
+          float4* dst = reinterpret_cast<float4*>(my_o + c * 32);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            __nv_bfloat162 h2 = __floats2bfloat162_rn(ov[2 * i] * norm, ov[2 * i + 1] * norm);
-            w[i] = *reinterpret_cast<uint32_t*>(&h2);
+          for (int i = 0; i < 8; ++i) __stcg(dst + i, make_float4(ov[4 * i], ov[4 * i + 1], ov[4 * i + 2], ov[4 * i + 3]));
+        }
+        __stcg(reinterpret_cast<float2*>(my_ml), make_float2(m_used, l_run));
+      }
+      __threadfence();
+      named_bar_sync(1, NQ * TQ);
+      volatile int* last_flag = abort_flag + 1;
+      if (threadIdx.x == 64) {
+        const unsigned old = atomicAdd(p.ws_count + slot, 1u);
+        __threadfence();
+        *last_flag = (int)(old & 1u);
+      }
+      named_bar_sync(1, NQ * TQ);
+      if (*last_flag && ok) {
+        const int other = piece ^ 1;
+        const float* ot_o = p.ws_o + ((int64_t)(slot * 2 + other) * NQ * TQ + prow) * HD;
+        const float2 ot_ml = __ldcg(reinterpret_cast<const float2*>(p.ws_ml + ((int64_t)(slot * 2 + other) * NQ * TQ + prow) * 2));
+        // Combine in piece order (lower keys first) whichever CTA is last.
+        const float m0 = piece == 0 ? m_used : ot_ml.x, m1 = piece == 0 ? ot_ml.x : m_used;
+        const float l0 = piece == 0 ? l_run : ot_ml.y, l1 = piece == 0 ? ot_ml.y : l_run;
+        const float mm = fmaxf(m0, m1);
+        const float w0 = m0 == -INFINITY ? 0.0f : ex2_f32(m0 - mm);
+        const float w1 = m1 == -INFINITY ? 0.0f : ex2_f32(m1 - mm);
+        const float norm = __fdiv_rn(*p.v_global, __fadd_rn(__fmul_rn(l0, w0), __fmul_rn(l1, w1)));
+        const float w_own = piece == 0 ? w0 : w1, w_other = piece == 0 ? w1 : w0;
+#pragma unroll 1
+        for (int c = 0; c < HD / 32; ++c) {
+          float ov[32], xv[32];
+          __syncwarp();
+          tmem_ld32(o_addr + c * 32, ov);
+          const float4* src = reinterpret_cast<const float4*>(ot_o + c * 32);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 v = __ldcg(src + i);
+            xv[4 * i] = v.x, xv[4 * i + 1] = v.y, xv[4 * i + 2] = v.z, xv[4 * i + 3] = v.w;
           }
-          uint4* o = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) o[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          if (qrow < p.rows) {
+            if (piece == 0)
+              store_out_row(orow + c * 32, ov, norm, xv, w_own, w_other);
+            else
+              store_out_row(orow + c * 32, xv, norm, ov, w_other, w_own);
+          }
         }
       }
     }
@@ -496,6 +601,36 @@ bool make_map16(CUtensorMap* map, CUtensorMapDataType type, const void* base, in
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+int sm_count(int dev) {
+  static int sms[64] = {};
+  if (!sms[dev]) {
+    int count = 0;
+    if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || count < 1) return 0;
+    sms[dev] = count;
+  }
+  return sms[dev];
+}
+
+// How many of the lightest units to split into two key-range halves.  One CTA
+// per SM (the kernel holds all 512 TMEM columns), so `units` CTAs run in
+// ceil(units / sms) waves and the last wave is partly idle; splitting that
+// wave's units in two halves its length.  With fewer units than SMs, split as
+// many as there are idle SMs.  Every split unit needs >= 2 key tiles.
+// split_plan never splits more than half the SM count.
+int max_split_slots(int sms) { return sms / 2; }
+
+int split_plan(int units, int sms, int lightest_tiles, int slots_available) {
+  if (sms < 1 || lightest_tiles < 2) return 0;
+  int k = 0;
+  if (units < sms) {
+    k = units < sms - units ? units : sms - units;
+  } else {
+    const int r = units % sms;
+    if (r > 0 && r <= sms / 2) k = r;
+  }
+  return k < slots_available ? k : slots_available;
+}
+
 template <int HD>
 int launch_attention(const QiAttention* a, cudaStream_t stream) {
   CUtensorMap mq, mk, mv;
@@ -513,6 +648,7 @@ int launch_attention(const QiAttention* a, cudaStream_t stream) {
   int cur_dev = 0;
   cudaGetDevice(&cur_dev);
   if (cur_dev < 0 || cur_dev >= 64) return (int)cudaErrorInvalidDevice;
+  const int sms = sm_count(cur_dev);
   if (!configured[cur_dev]) {
     const cudaError_t e =
         cudaFuncSetAttribute(attn_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, Geometry<HD>::SMEM);
@@ -532,7 +668,26 @@ int launch_attention(const QiAttention* a, cudaStream_t stream) {
   p.softmax_scale = a->softmax_scale;
   p.status = a->status;
   p.q_blocks = (a->rows + NQ * TQ - 1) / (NQ * TQ);
-  attn_kernel<HD><<<p.q_blocks * a->qheads, 320, Geometry<HD>::SMEM, stream>>>(mq, mk, mv, p);
+  const int units = p.q_blocks * a->qheads;
+  int slots_available = 0;
+  if (a->workspace && a->workspace_bytes > 0) {
+    int lo = 0, hi = units < kMaxSlots ? units : kMaxSlots;  // largest slot count whose workspace fits
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) / 2;
+      if (ws_bytes(mid, HD) <= a->workspace_bytes) lo = mid; else hi = mid - 1;
+    }
+    slots_available = lo;
+  }
+  const int lightest_tiles = (a->history + (a->rows < NQ * TQ ? a->rows : NQ * TQ) + TK - 1) / TK;
+  const int split = split_plan(units, sms, lightest_tiles, slots_available);
+  p.split_first = units - split;
+  if (split) {
+    uint8_t* ws = static_cast<uint8_t*>(a->workspace);
+    p.ws_count = reinterpret_cast<unsigned*>(ws);
+    p.ws_ml = reinterpret_cast<float*>(ws + ws_count_bytes(split));
+    p.ws_o = reinterpret_cast<float*>(ws + ws_count_bytes(split) + ws_ml_bytes(split));
+  }
+  attn_kernel<HD><<<units + split, 320, Geometry<HD>::SMEM, stream>>>(mq, mk, mv, p);
   return (int)cudaPeekAtLastError();
 }
 
@@ -548,6 +703,20 @@ extern "C" int qi_prefill_attention(const QiAttention* a, cudaStream_t stream) {
   if (a->kv_tokens < a->history + a->rows || a->vt_row < a->kv_tokens || a->vt_row % 8 || a->q_row % 8 ||
       a->out_row % 8 || a->q_row < a->qheads * hd || a->out_row < a->qheads * hd)
     return (int)cudaErrorInvalidValue;
-  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->vt) || !aligned16(a->out)) return (int)cudaErrorInvalidValue;
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->vt) || !aligned16(a->out) ||
+      (a->workspace && (reinterpret_cast<uintptr_t>(a->workspace) & 255)))
+    return (int)cudaErrorInvalidValue;
   return a->head_dim == 64 ? launch_attention<64>(a, stream) : launch_attention<128>(a, stream);
+}
+
+extern "C" int qi_prefill_attention_workspace_bytes(int head_dim, int64_t* bytes) {
+  if (!bytes || (head_dim != 64 && head_dim != 128)) return (int)cudaErrorInvalidValue;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+  const int sms = sm_count(dev);
+  if (!sms) return (int)cudaErrorInvalidDevice;
+  *bytes = ws_bytes(max_split_slots(sms), head_dim);
+  return 0;
 }

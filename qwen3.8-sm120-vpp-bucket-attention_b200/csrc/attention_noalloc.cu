@@ -10,7 +10,8 @@
 //
 // Cost and limits:
 //   * every GPU that loads this library holds kScratchBytes (32 MiB) of device
-//     memory for this array until the process exits;
+//     memory for this array, plus the attention kernel's key-range split
+//     workspace (kSplitBytes, about 21 MB), until the process exits;
 //   * a call is limited to what fits in it: Hkv * tokens * D * 2 bytes of K
 //     plus Hkv * D * round_up(tokens, 64) * 2 bytes of V^T (27B shape, 8 KV
 //     heads x 128: up to 8192 tokens of history + chunk); larger requests are
@@ -34,21 +35,33 @@ namespace {
 constexpr size_t kScratchBytes = size_t(32) << 20;
 __device__ __align__(256) unsigned char g_attention_scratch[kScratchBytes];
 
+// Key-range split workspace of the attention kernel (QiAttention.workspace):
+// room for 80 split units of head_dim 128 (the kernel splits at most half
+// the SM count; a device with more than 160 SMs gets fewer splits).  Zero at
+// load, as the kernel requires; the kernel keeps its counters consistent.
+constexpr size_t kSplitBytes = size_t(4096) + size_t(80) * 2 * 256 * 2 * 4 + size_t(80) * 2 * 256 * 128 * 4;
+__device__ __align__(256) unsigned char g_split_workspace[kSplitBytes];
+
 constexpr int kMaxDevices = 64;
 void* g_scratch_addr[kMaxDevices] = {};
+void* g_split_addr[kMaxDevices] = {};
 std::mutex g_scratch_mutex;
 
 // Device address of the scratch array on the current device (looked up once
 // per device; the host-side symbol itself is not a device address).
-cudaError_t scratch_address(int device, void** out) {
+cudaError_t scratch_address(int device, void** out, void** split) {
   std::lock_guard<std::mutex> lock(g_scratch_mutex);
   if (!g_scratch_addr[device]) {
-    void* ptr = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_attention_scratch);
+    void *ptr = nullptr, *ws = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_attention_scratch);
+    if (e != cudaSuccess) return e;
+    e = cudaGetSymbolAddress(&ws, g_split_workspace);
     if (e != cudaSuccess) return e;
     g_scratch_addr[device] = ptr;
+    g_split_addr[device] = ws;
   }
   *out = g_scratch_addr[device];
+  *split = g_split_addr[device];
   return cudaSuccess;
 }
 
@@ -72,8 +85,8 @@ extern "C" int qi_paged_prefill_attention_noalloc(const QiKvView* kv, const int3
   cudaError_t e = cudaGetDevice(&device);
   if (e != cudaSuccess) return (int)e;
   if (device < 0 || device >= kMaxDevices) return (int)cudaErrorInvalidDevice;
-  void* scratch = nullptr;
-  e = scratch_address(device, &scratch);
+  void *scratch = nullptr, *split = nullptr;
+  e = scratch_address(device, &scratch, &split);
   if (e != cudaSuccess) return (int)e;
   unsigned char* base = static_cast<unsigned char*>(scratch);
   int rc = qi_kv_dequant(kv, block_table, (int)tokens, base, base + k_span, vt_row, stream);
@@ -96,5 +109,7 @@ extern "C" int qi_paged_prefill_attention_noalloc(const QiKvView* kv, const int3
   a.out_row = out_row;
   a.vt_row = vt_row;
   a.softmax_scale = softmax_scale;
+  a.workspace = split;
+  a.workspace_bytes = (int64_t)kSplitBytes;
   return qi_prefill_attention(&a, stream);
 }

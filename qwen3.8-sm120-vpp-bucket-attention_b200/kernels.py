@@ -266,11 +266,35 @@ def kv_dequant(kv, block_table, tokens, *, k_out=None, vt_out=None):
     return k_out, vt_out
 
 
+_ATTN_WORKSPACE = {}
+
+
+def attention_workspace(device, head_dim):
+    """Zero-filled key-range split workspace for :func:`prefill_attention` on
+    ``device`` (one per device and head_dim, cached; calls on one stream may
+    share it)."""
+    device = torch.device(device)
+    key = (device.index if device.index is not None else torch.cuda.current_device(), head_dim)
+    ws = _ATTN_WORKSPACE.get(key)
+    if ws is None:
+        nbytes = ct.c_int64(0)
+        with torch.cuda.device(key[0]):
+            N.check(N.lib().qi_prefill_attention_workspace_bytes(head_dim, ct.byref(nbytes)),
+                    "qi_prefill_attention_workspace_bytes")
+        ws = torch.zeros(nbytes.value, dtype=torch.uint8, device=torch.device("cuda", key[0]))
+        _ATTN_WORKSPACE[key] = ws
+    return ws
+
+
 def prefill_attention(q, k, vt, *, history, qheads, kvheads, head_dim, k_global, v_global, out=None,
-                      softmax_scale=None, status=None, kv_tokens=None):
+                      softmax_scale=None, status=None, kv_tokens=None, workspace=None):
     """Causal GQA attention of ``rows`` queries at positions history.. over
-    keys 0 .. history+rows-1 held as f16 K / V^T (from :func:`kv_dequant`)."""
+    keys 0 .. history+rows-1 held as f16 K / V^T (from :func:`kv_dequant`).
+    ``workspace``: the key-range split workspace (default: the device's cached
+    one from :func:`attention_workspace`)."""
     _cuda(q, k, vt, k_global, v_global)
+    if workspace is None:
+        workspace = attention_workspace(q.device, head_dim)
     rows = q.shape[0]
     if out is None:
         out = torch.empty((rows, qheads * head_dim), dtype=torch.bfloat16, device=q.device)
@@ -283,6 +307,7 @@ def prefill_attention(q, k, vt, *, history, qheads, kvheads, head_dim, k_global,
     p.qheads, p.kvheads, p.head_dim = qheads, kvheads, head_dim
     p.q_row, p.out_row, p.vt_row = q.stride(0), out.stride(0), vt.shape[2]
     p.softmax_scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(head_dim)
+    p.workspace, p.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
     N.check(_run("attention", 4 * qheads * head_dim * (rows * history + rows * (rows + 1) // 2), "FLOP", q.device, lambda: N.lib().qi_prefill_attention(ct.byref(p), _stream(q.device))), "qi_prefill_attention")
     return out
 

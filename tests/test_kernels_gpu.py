@@ -276,10 +276,14 @@ def test_kv_dequant_exact(K, tokens, d):
     assert np.array_equal(vt.float().cpu().numpy()[:, :, :tokens], v_ref.transpose(1, 2, 0))
 
 
+@pytest.mark.parametrize("split", [True, False])
 @pytest.mark.parametrize("rows,history,qh,kvh,d", [(128, 0, 16, 4, 64), (200, 300, 16, 4, 64),
                                                    (512, 0, 64, 8, 128), (77, 1500, 64, 8, 128),
-                                                   (1, 4000, 64, 8, 128)])
-def test_prefill_attention_matches_fp32(K, rows, history, qh, kvh, d):
+                                                   (1, 4000, 64, 8, 128), (2048, 1024, 64, 8, 128)])
+def test_prefill_attention_matches_fp32(K, rows, history, qh, kvh, d, split):
+    """split=True: the default workspace, so units of the last partly idle
+    wave (or all units, when there are fewer than SMs) run as two key-range
+    halves combined in the kernel; split=False: no workspace, no split."""
     tokens = history + rows
     g = torch.Generator().manual_seed(81 + rows)
     q = (torch.randn(rows, qh * d, generator=g)).to(torch.bfloat16)
@@ -290,9 +294,12 @@ def test_prefill_attention_matches_fp32(K, rows, history, qh, kvh, d):
     vt = torch.zeros(kvh, d, vt_row, dtype=torch.float16)
     vt[:, :, :tokens] = v.transpose(1, 2)
     kg, vg = 1.0 / 64, 1.0 / 64
-    out = K.prefill_attention(q.to(DEV), k.to(DEV), vt.to(DEV), history=history, qheads=qh, kvheads=kvh,
-                              head_dim=d, k_global=torch.tensor([kg], device=DEV),
-                              v_global=torch.tensor([vg], device=DEV))
+    ws = None if split else torch.empty(0, dtype=torch.uint8, device=DEV)
+    args = dict(history=history, qheads=qh, kvheads=kvh, head_dim=d, k_global=torch.tensor([kg], device=DEV),
+                v_global=torch.tensor([vg], device=DEV), workspace=ws)
+    out = K.prefill_attention(q.to(DEV), k.to(DEV), vt.to(DEV), **args)
+    again = K.prefill_attention(q.to(DEV), k.to(DEV), vt.to(DEV), **args)
+    assert torch.equal(out, again)  # the split's arrival counters reset themselves
     ref = OM.attention(q.float().numpy(), (k.float() * kg).transpose(0, 1).contiguous().numpy(),
                        (v.float() * vg).transpose(0, 1).contiguous().numpy(), history,
                        OM.Shape(1, qh * d, qh, kvh, d, 4 * d))
