@@ -196,6 +196,22 @@ QI_DEV void tmem_st32u(uint32_t taddr, const uint32_t* v) {
       : "memory");
 }
 
+// Max of 64 values in four independent chains (short dependency chains).
+QI_DEV float max64(const float* v) {
+  float a = fmax3(v[0], v[1], v[2]), b = fmax3(v[3], v[4], v[5]), c = fmax3(v[6], v[7], v[8]),
+        d = fmax3(v[9], v[10], v[11]);
+#pragma unroll
+  for (int i = 12; i < 60; i += 8) {
+    a = fmax3(a, v[i], v[i + 1]);
+    b = fmax3(b, v[i + 2], v[i + 3]);
+    c = fmax3(c, v[i + 4], v[i + 5]);
+    d = fmax3(d, v[i + 6], v[i + 7]);
+  }
+  a = fmax3(a, v[60], v[61]);
+  b = fmax3(b, v[62], v[63]);
+  return fmax3(fmaxf(a, b), c, d);
+}
+
 QI_DEV void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
@@ -264,7 +280,7 @@ __global__ void __launch_bounds__(320, 1)
     prefetch_tensormap(&tk);
     prefetch_tensormap(&tv);
     mbar_init(q_full, 1);
-    mbar_init(q_ready, NQ * 128);
+    mbar_init(q_ready, NQ * 4);  // one arrival per softmax warp
     for (int i = 0; i < 2; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
@@ -273,7 +289,7 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int i = 0; i < NQ; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[i], 4);  // one arrival per softmax warp
       mbar_init(&pv_done[i], 1);
     }
     *abort_flag = 0;
@@ -393,7 +409,8 @@ __global__ void __launch_bounds__(320, 1)
       }
     }
     fence_proxy_async_smem();
-    mbar_arrive(q_ready);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(q_ready);
     const float scale2 = __fmul_rn(__fmul_rn(p.softmax_scale, *p.k_global), 1.4426950408889634f);
     float m_used = -INFINITY, l_run = 0.0f;
     for (int j = 0; ok && j < ntiles; ++j) {
@@ -418,8 +435,7 @@ __global__ void __launch_bounds__(320, 1)
           for (int c = 0; c < 64; ++c)
             if (kbase + h * 64 + c > qpos) sv[c] = -INFINITY;
         }
-#pragma unroll
-        for (int c = 0; c < 64; c += 2) mx = fmax3(mx, sv[c], sv[c + 1]);
+        mx = fmaxf(mx, max64(sv));
       }
       const float m_tile = mx * scale2;
       float corr = 1.0f;
@@ -436,7 +452,7 @@ __global__ void __launch_bounds__(320, 1)
       }
       const float m_sub = m_used == -INFINITY ? 0.0f : m_used;
       const float2 sc2 = make_float2(scale2, scale2), nm2 = make_float2(-m_sub, -m_sub);
-      float2 acc = make_float2(0.0f, 0.0f);
+      float2 acc = make_float2(0.0f, 0.0f), acc_b = make_float2(0.0f, 0.0f);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         float sv[64];
@@ -459,14 +475,14 @@ __global__ void __launch_bounds__(320, 1)
           } else {
             e = make_float2(ex2_f32(d.x), ex2_f32(d.y));
           }
-          acc = fadd2(acc, e);
+          if (c & 1) acc_b = fadd2(acc_b, e); else acc = fadd2(acc, e);
           pw[c] = pack_f16x2(e.x, e.y);
         }
         // P for keys [64h, 64h+64) -> S columns [32h, 32h+32); pass 2 of the
         // second half reads columns 64..127, which this store does not touch.
         tmem_st32u(s_addr + h * 32, pw);
       }
-      const float sum = acc.x + acc.y;
+      const float sum = (acc.x + acc.y) + (acc_b.x + acc_b.y);
       l_run = l_run * corr + sum;
       // PV_t of the previous key tile has completed (the commit that signalled
       // this S_t covers it), so O may be rescaled.
@@ -482,7 +498,8 @@ __global__ void __launch_bounds__(320, 1)
       }
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
-      mbar_arrive(&p_full[t]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
     }
     if (ok) ok = mbar_wait(&pv_done[t], 0, abort_flag, p.status);
     tc_fence_after();
@@ -619,8 +636,12 @@ int sm_count(int dev) {
 // split_plan never splits more than half the SM count.
 int max_split_slots(int sms) { return sms / 2; }
 
+// Short units are not split: below kMinSplitTiles key tiles the second CTA's
+// fixed cost (Q load, first QK^T, the combine) outweighs the shorter wave.
+constexpr int kMinSplitTiles = 24;
+
 int split_plan(int units, int sms, int lightest_tiles, int slots_available) {
-  if (sms < 1 || lightest_tiles < 2) return 0;
+  if (sms < 1 || lightest_tiles < kMinSplitTiles) return 0;
   int k = 0;
   if (units < sms) {
     k = units < sms - units ? units : sms - units;
