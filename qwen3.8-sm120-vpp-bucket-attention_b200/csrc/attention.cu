@@ -256,7 +256,8 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* s_full = bars + 10;   // [NQ]
   uint64_t* p_full = bars + 12;   // [NQ]
   uint64_t* pv_done = bars + 14;  // [NQ]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* p_half = bars + 16;   // [NQ] P of keys 0..63 of the tile stored
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -290,6 +291,7 @@ __global__ void __launch_bounds__(320, 1)
     for (int i = 0; i < NQ; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);  // one arrival per softmax warp
+      mbar_init(&p_half[i], 4);
       mbar_init(&pv_done[i], 1);
     }
     *abort_flag = 0;
@@ -324,7 +326,8 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // Issue order: S0_0 S1_0 | PV0_0 S0_1 PV1_0 S1_1 | PV0_1 S0_2 ... so that
+      // Issue order: S0_0 S1_0 | PV0_0 S0_1 PV1_0 S1_1 | PV0_1 S0_2 ... (each PV
+      // in two halves of 64 keys, the first as soon as its P is stored) so that
       // the softmax of one tile overlaps the other tile's PV + S pair.  S_t(j+1)
       // overwrites the TMEM columns that PV_t(j), issued just before it by this
       // thread, reads P_t(j) from; tcgen05.mma operations issued by one thread
@@ -346,11 +349,11 @@ __global__ void __launch_bounds__(320, 1)
         }
         tc_commit(&s_full[t]);
       };
-      auto issue_pv = [&](int t, int j) {
+      auto issue_pv = [&](int t, int j, int h) {  // keys 64h .. 64h+63 of the tile
         const uint32_t v_base = smem_u32(sV + (j & 1) * V_BYTES);
         const uint32_t a_p = tmem + (t ? G::S_COL1 : G::S_COL0), d_o = tmem + (t ? G::O_COL1 : G::O_COL0);
 #pragma unroll
-        for (int kk = 0; kk < TK / 16; ++kk) {
+        for (int kk = 4 * h; kk < 4 * h + 4; ++kk) {
           const uint32_t voff = (kk >> 2) * V_ATOM + (kk & 3) * 32;
           mma_f16_ts(d_o, a_p + kk * 8, sdesc_kmajor_sw128(v_base + voff), idesc_o, (j | kk) ? 1u : 0u);
         }
@@ -366,13 +369,19 @@ __global__ void __launch_bounds__(320, 1)
         const bool more = j + 1 < ntiles;
         if (!(ok = mbar_wait(&v_full[s], (j >> 1) & 1, abort_flag, p.status))) break;
         if (more && !(ok = mbar_wait(&k_full[s ^ 1], ((j + 1) >> 1) & 1, abort_flag, p.status))) break;
+        if (!(ok = mbar_wait(&p_half[0], j & 1, abort_flag, p.status))) break;
+        tc_fence_after();
+        issue_pv(0, j, 0);
         if (!(ok = mbar_wait(&p_full[0], j & 1, abort_flag, p.status))) break;
         tc_fence_after();
-        issue_pv(0, j);
+        issue_pv(0, j, 1);
         if (more) issue_s(0, j + 1);
+        if (!(ok = mbar_wait(&p_half[1], j & 1, abort_flag, p.status))) break;
+        tc_fence_after();
+        issue_pv(1, j, 0);
         if (!(ok = mbar_wait(&p_full[1], j & 1, abort_flag, p.status))) break;
         tc_fence_after();
-        issue_pv(1, j);
+        issue_pv(1, j, 1);
         tc_commit(&v_empty[s]);
         if (more) {
           issue_s(1, j + 1);
@@ -450,6 +459,19 @@ __global__ void __launch_bounds__(320, 1)
         m_used = m_tile;
         rescale = true;
       }
+      // PV_t of the previous key tile has completed (the commit that signalled
+      // this S_t covers it), so O may be rescaled -- before the first half of
+      // P is published, since PV_t(j) starts on it.
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+        for (int c = 0; c < HD / 32; ++c) {
+          float ov[32];
+          tmem_ld32(o_addr + c * 32, ov);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ov[i] *= corr;
+          tmem_st32(o_addr + c * 32, ov);
+        }
+      }
       const float m_sub = m_used == -INFINITY ? 0.0f : m_used;
       const float2 sc2 = make_float2(scale2, scale2), nm2 = make_float2(-m_sub, -m_sub);
       float2 acc = make_float2(0.0f, 0.0f), acc_b = make_float2(0.0f, 0.0f);
@@ -481,25 +503,15 @@ __global__ void __launch_bounds__(320, 1)
         // P for keys [64h, 64h+64) -> S columns [32h, 32h+32); pass 2 of the
         // second half reads columns 64..127, which this store does not touch.
         tmem_st32u(s_addr + h * 32, pw);
+        // Publish each half as soon as it is stored: the MMA thread runs the
+        // PV of keys 0..63 while the second half is being computed.
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(h == 0 ? &p_half[t] : &p_full[t]);
       }
       const float sum = (acc.x + acc.y) + (acc_b.x + acc_b.y);
       l_run = l_run * corr + sum;
-      // PV_t of the previous key tile has completed (the commit that signalled
-      // this S_t covers it), so O may be rescaled.
-      if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll 1
-        for (int c = 0; c < HD / 32; ++c) {
-          float ov[32];
-          tmem_ld32(o_addr + c * 32, ov);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) ov[i] *= corr;
-          tmem_st32(o_addr + c * 32, ov);
-        }
-      }
-      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
     }
     if (ok) ok = mbar_wait(&pv_done[t], 0, abort_flag, p.status);
     tc_fence_after();
