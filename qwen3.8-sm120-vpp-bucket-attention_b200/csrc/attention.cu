@@ -5,9 +5,9 @@
 // (e2m1 x e4m3 products are exact in f16); the fp32 global multipliers of K
 // and V are folded into the softmax scale and the output normalisation.  S and
 // O accumulate in fp32 in tensor memory; P = 2^(s*scale*log2e - m) is formed
-// with packed f16 exponentials and written back into the S columns of tensor
-// memory, from where the PV MMA reads it as its A operand (no shared-memory
-// round trip).
+// in fp32 (MUFU ex2), packed to f16 pairs and written back into the S columns
+// of tensor memory, from where the PV MMA reads it as its A operand (no
+// shared-memory round trip).
 //
 // One CTA = 256 query rows (two 128-row tiles Q0, Q1) of one query head; 10 warps:
 //   warp 0      : TMA producer (Q once; K and V^T tiles of 128 keys, 2 stages),
@@ -94,15 +94,6 @@ QI_DEV uint32_t pack_f16x2(float lo, float hi) {
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
 }
-QI_DEV uint32_t ex2_f16x2(uint32_t x) {
-  uint32_t r;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(x));
-  return r;
-}
-QI_DEV float2 unpack_f16x2(uint32_t v) {
-  __half2 h = *reinterpret_cast<__half2*>(&v);
-  return __half22float2(h);
-}
 QI_DEV float ex2_f32(float x) {
   float r;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
@@ -123,23 +114,6 @@ QI_DEV void tmem_ld32_nowait(uint32_t taddr, float* v) {
       : "r"(taddr));
 }
 QI_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// 2^x on the FMA and integer pipes, for x <= 8 (P is rounded to f16 anyway):
-// n = rint(x) via the 1.5*2^23 rounding constant, f = x - n in [-1/2, 1/2],
-// 2^f by a degree-3 polynomial (weighted least-squares fit of 2^f on
-// [-1/2, 1/2] at Chebyshev nodes; relative error 1.2e-4, under the f16
-// rounding of P), exponent added as n << 23.
-// Offloads part of the exponentials from the 16-per-clock MUFU unit.
-QI_DEV float ex2_poly(float x) {
-  x = fmaxf(x, -127.0f);
-  const float t = __fadd_rn(x, 12582912.0f);
-  const float n = __fsub_rn(t, 12582912.0f);
-  const float f = __fsub_rn(x, n);
-  float p = fmaf(f, 0x1.c5fb94p-5f, 0x1.f00c82p-3f);
-  p = fmaf(p, f, 0x1.62eb0cp-1f);
-  p = fmaf(p, f, 1.0f);
-  return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
-}
 
 // Packed fp32 pair arithmetic (one instruction for two lanes' worth of work).
 QI_DEV float2 ffma2(float2 a, float2 b, float2 c) {
@@ -165,26 +139,6 @@ QI_DEV float fmax3(float a, float b, float c) {
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
-// ex2_poly on a pair with packed arithmetic.
-QI_DEV float2 ex2_poly2(float2 x) {
-  x.x = fmaxf(x.x, -127.0f);
-  x.y = fmaxf(x.y, -127.0f);
-  const float2 t = fadd2(x, make_float2(12582912.0f, 12582912.0f));
-  const float2 n = fadd2(t, make_float2(-12582912.0f, -12582912.0f));
-  const float2 f = ffma2(n, make_float2(-1.0f, -1.0f), x);
-  float2 p = ffma2(f, make_float2(0x1.c5fb94p-5f, 0x1.c5fb94p-5f), make_float2(0x1.f00c82p-3f, 0x1.f00c82p-3f));
-  p = ffma2(p, f, make_float2(0x1.62eb0cp-1f, 0x1.62eb0cp-1f));
-  p = ffma2(p, f, make_float2(1.0f, 1.0f));
-  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
-                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
-}
-
-QI_DEV uint32_t hadd2(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-
 QI_DEV void tmem_st32u(uint32_t taddr, const uint32_t* v) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
@@ -491,12 +445,10 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
           const float2 d = ffma2(make_float2(sv[2 * c], sv[2 * c + 1]), sc2, nm2);
-          float2 e;
-          if ((c & 3) == 3) {  // one pair in four on the FMA pipe, the rest on MUFU
-            e = ex2_poly2(d);
-          } else {
-            e = make_float2(ex2_f32(d.x), ex2_f32(d.y));
-          }
+          // All exponentials on MUFU: the softmax is latency-bound here, and
+          // moving a share to an FMA-pipe polynomial (Cody-Waite split plus a
+          // cubic) measured slower at every share tried (1/8 .. 1/2).
+          const float2 e = make_float2(ex2_f32(d.x), ex2_f32(d.y));
           if (c & 1) acc_b = fadd2(acc_b, e); else acc = fadd2(acc, e);
           pw[c] = pack_f16x2(e.x, e.y);
         }
