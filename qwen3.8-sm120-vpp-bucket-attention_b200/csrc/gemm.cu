@@ -3,18 +3,18 @@
 //
 //   D[m, n] = sum_k A[m, k] * B[n, k]     (A: activations, B: weights, both K-major)
 //
-// Persistent, warp-specialised: one CTA per SM walks 128 x 256 output tiles
-// (M tiles fastest, so the CTAs in flight share weight tiles through L2 and
-// each weight byte is read from HBM about once).
-//   warp 0      : TMA producer (A and B tiles, 128-byte swizzle; block scales by
-//                 untiled bulk copies of whole 512-byte swizzle atoms) running
-//                 ahead across tile boundaries through a 4-stage smem ring,
-//   warp 1      : TMEM allocator and the single thread issuing tcgen05.cp (scale
-//                 factors smem -> TMEM, own columns per stage) and tcgen05.mma,
-//   warps 2..9  : epilogue: two warps per TMEM lane quarter, each reading half
-//                 of the tile's columns; the accumulator is released as soon as
-//                 it is in registers, so the fused epilogue math and the global
-//                 stores overlap the next tile's MMAs.
+// All three kernels are persistent and warp-specialised: a CTA (or CTA pair)
+// per SM walks the output tiles (M tiles fastest, so the CTAs in flight share
+// weight tiles through L2 and each weight byte is read from HBM about once);
+// a TMA producer runs ahead across tile boundaries through a shared-memory
+// ring; one thread issues tcgen05.mma into a 256-column TMEM accumulator; the
+// epilogue warps (two per TMEM lane quarter, each on half of the tile's
+// columns) release the accumulator as soon as it is in registers, so the
+// fused epilogue math and the global stores overlap the next tile's MMAs.
+//   gemm_sfw_kernel   NVFP4, 128 x 256 tiles, block scales written to TMEM by
+//                     four scale-writer warps (tcgen05.st), 16 warps;
+//   gemm_pair_kernel  E4M3 with M > 128: CTA pairs, 2-SM MMAs, 256 x 256 tiles;
+//   gemm_kernel       E4M3 with M <= 128: 128 x 256 tiles, 10 warps.
 #include <mutex>
 
 #include "common.cuh"
@@ -30,15 +30,12 @@ constexpr int A_BYTES = BM * BKB;
 constexpr int B_BYTES = BN * BKB;
 constexpr int SFA_BYTES = 2048;  // 128 rows x 16 scales (4 atoms of 512 B)
 constexpr int SFB_BYTES = 4096;  // 256 rows x 16 scales
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;  // NVFP4 stage
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
-constexpr int THREADS = 320;
+constexpr int THREADS = 320;     // gemm_kernel and gemm_pair_kernel
 constexpr int EPI_THREADS = 256;
 constexpr uint32_t TMEM_COLS = 512;
-// Scale factors get their own TMEM columns per pipeline stage (16 for A, 32
-// for B), so copying the next stage's scales never waits on MMAs that still
-// read the previous ones.
-constexpr uint32_t ACC_COL = 0, SFA_COL = 256, SFB_COL = 256 + STAGES * 16;
+constexpr uint32_t ACC_COL = 0;
 
 struct Params {
   int m, n, kt;  // kt: number of 128-byte K tiles
@@ -60,16 +57,69 @@ struct Params {
   int* status;
 };
 
-template <bool kFp4, int kEpi>
+// Fused epilogue for one thread's row: v holds its 128 accumulator columns
+// (half h of the 256-column tile starting at n0; for SwiGLU the 64 gate and
+// 64 up columns of output channels (n0/2 + 64h ..)).
+template <int kEpi>
+__device__ __forceinline__ void epilogue_rows(const Params& p, float* v, int row, int n0, int half, float alpha) {
+  if constexpr (kEpi == QI_EPI_SWIGLU_NVFP4) {
+    const float g = *p.act_global;
+    const int64_t gp = p.act_gp;
+    const int ch0 = (n0 >> 1) + half * 64;  // first output channel of this thread's half
+#pragma unroll
+    for (int j = 0; j < 64; ++j) {
+      const float gg = bf16r(__fmul_rn(v[j], alpha));
+      const float uu = bf16r(__fmul_rn(v[64 + j], alpha));
+      v[j] = bf16r(__fmul_rn(silu_f(gg), uu));
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint2 packed;
+      const uint32_t code = nvfp4_quant16(v + 16 * q, g, packed);
+      const int ch = ch0 + 16 * q;
+      *reinterpret_cast<uint2*>(p.act_q + (int64_t)row * p.act_ld + (ch >> 1)) = packed;
+      p.act_sf[sf_offset(row, ch >> 4, gp)] = (uint8_t)code;
+    }
+  } else if constexpr (kEpi == QI_EPI_F32) {
+    float* o = static_cast<float*>(p.out) + (int64_t)row * p.ldo + n0 + half * 128;
+#pragma unroll
+    for (int j = 0; j < 128; j += 4)
+      *reinterpret_cast<float4*>(o + j) = make_float4(__fmul_rn(v[j], alpha), __fmul_rn(v[j + 1], alpha),
+                                                      __fmul_rn(v[j + 2], alpha), __fmul_rn(v[j + 3], alpha));
+  } else {
+    const int col0 = n0 + half * 128;
+    float rs = 1.0f;
+    if constexpr (kEpi == QI_EPI_BF16_ROWCOL) rs = p.row_scale[row];
+    uint4* o = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo + col0);
+#pragma unroll
+    for (int j = 0; j < 128; j += 8) {
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float a, b;
+        if constexpr (kEpi == QI_EPI_BF16_ROWCOL) {
+          a = __fmul_rn(__fmul_rn(v[j + 2 * i], rs), p.col_scale[col0 + j + 2 * i]);
+          b = __fmul_rn(__fmul_rn(v[j + 2 * i + 1], rs), p.col_scale[col0 + j + 2 * i + 1]);
+        } else {
+          a = __fmul_rn(v[j + 2 * i], alpha);
+          b = __fmul_rn(v[j + 2 * i + 1], alpha);
+        }
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(a, b);
+        w[i] = *reinterpret_cast<uint32_t*>(&h2);
+      }
+      o[j / 8] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+template <int kEpi>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + STAGES * A_BYTES;
-  uint8_t* sSFA = sB + STAGES * B_BYTES;
-  uint8_t* sSFB = sSFA + STAGES * SFA_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sSFB + STAGES * SFB_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 1;
@@ -99,7 +149,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint32_t tx = A_BYTES + B_BYTES + (kFp4 ? SFA_BYTES + SFB_BYTES : 0);
+      constexpr uint32_t tx = A_BYTES + B_BYTES;
       uint32_t it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
@@ -110,20 +160,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           mbar_expect_tx(&full[s], tx);
           tma_load_2d(sA + s * A_BYTES, &tma_a, &full[s], kt * BKB, m0);
           tma_load_2d(sB + s * B_BYTES, &tma_b, &full[s], kt * BKB, n0);
-          if constexpr (kFp4) {
-            bulk_load(sSFA + s * SFA_BYTES, p.sfa + (int64_t)(m0 >> 7) * p.sfa_block + (int64_t)kt * 2048, 2048,
-                      &full[s]);
-            bulk_load(sSFB + s * SFB_BYTES, p.sfb + (int64_t)(n0 >> 7) * p.sfb_block + (int64_t)kt * 2048, 2048,
-                      &full[s]);
-            bulk_load(sSFB + s * SFB_BYTES + 2048,
-                      p.sfb + (int64_t)((n0 >> 7) + 1) * p.sfb_block + (int64_t)kt * 2048, 2048, &full[s]);
-          }
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = kFp4 ? idesc_nvfp4(BN) : idesc_e4m3(BN);
+      constexpr uint32_t idesc = idesc_e4m3(BN);
       uint32_t it = 0, tcount = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, ++tcount) {
@@ -136,28 +178,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (!(ok = mbar_wait(&full[s], (it / STAGES) & 1, abort_flag, p.status))) break;
           tc_fence_after();
           const uint32_t a_base = smem_u32(sA + s * A_BYTES), b_base = smem_u32(sB + s * B_BYTES);
-          if constexpr (kFp4) {
-            // All of this stage's scale factors first, then its four MMAs.
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint32_t sfa_t = tmem + SFA_COL + s * 16 + kk * 4, sfb_t = tmem + SFB_COL + s * 32 + kk * 8;
-              tc_cp_sf(sfa_t, sdesc_sf_atom(smem_u32(sSFA + s * SFA_BYTES + kk * 512)));
-              tc_cp_sf(sfb_t, sdesc_sf_atom(smem_u32(sSFB + s * SFB_BYTES + kk * 512)));
-              tc_cp_sf(sfb_t + 4, sdesc_sf_atom(smem_u32(sSFB + s * SFB_BYTES + 2048 + kk * 512)));
-            }
-          }
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t adesc = sdesc_kmajor_sw128(a_base + kk * 32);
-            const uint64_t bdesc = sdesc_kmajor_sw128(b_base + kk * 32);
-            const uint32_t acc = (kt | kk) ? 1u : 0u;
-            if constexpr (kFp4) {
-              mma_nvfp4(tmem + ACC_COL, adesc, bdesc, idesc, tmem + SFA_COL + s * 16 + kk * 4,
-                        tmem + SFB_COL + s * 32 + kk * 8, acc);
-            } else {
-              mma_f8(tmem + ACC_COL, adesc, bdesc, idesc, acc);
-            }
-          }
+          for (int kk = 0; kk < 4; ++kk)
+            mma_f8(tmem + ACC_COL, sdesc_kmajor_sw128(a_base + kk * 32), sdesc_kmajor_sw128(b_base + kk * 32), idesc,
+                   (kt | kk) ? 1u : 0u);
           tc_commit(&empty[s]);
         }
         if (ok) tc_commit(acc_full);
@@ -196,54 +220,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_arrive(acc_empty);  // the accumulator may now take the next tile
       if (!ok) break;
       if (!in_range) continue;
-      if constexpr (kEpi == QI_EPI_SWIGLU_NVFP4) {
-        const float g = *p.act_global;
-        const int64_t gp = p.act_gp;
-        const int ch0 = (n0 >> 1) + half * 64;  // first output channel of this thread's half
-#pragma unroll
-        for (int j = 0; j < 64; ++j) {
-          const float gg = bf16r(__fmul_rn(v[j], alpha));
-          const float uu = bf16r(__fmul_rn(v[64 + j], alpha));
-          v[j] = bf16r(__fmul_rn(silu_f(gg), uu));
-        }
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint2 packed;
-          const uint32_t code = nvfp4_quant16(v + 16 * q, g, packed);
-          const int ch = ch0 + 16 * q;
-          *reinterpret_cast<uint2*>(p.act_q + (int64_t)row * p.act_ld + (ch >> 1)) = packed;
-          p.act_sf[sf_offset(row, ch >> 4, gp)] = (uint8_t)code;
-        }
-      } else if constexpr (kEpi == QI_EPI_F32) {
-        float* o = static_cast<float*>(p.out) + (int64_t)row * p.ldo + n0 + half * 128;
-#pragma unroll
-        for (int j = 0; j < 128; j += 4)
-          *reinterpret_cast<float4*>(o + j) = make_float4(__fmul_rn(v[j], alpha), __fmul_rn(v[j + 1], alpha),
-                                                          __fmul_rn(v[j + 2], alpha), __fmul_rn(v[j + 3], alpha));
-      } else {
-        const int col0 = n0 + half * 128;
-        float rs = 1.0f;
-        if constexpr (kEpi == QI_EPI_BF16_ROWCOL) rs = p.row_scale[row];
-        uint4* o = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo + col0);
-#pragma unroll
-        for (int j = 0; j < 128; j += 8) {
-          uint32_t w[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            float a, b;
-            if constexpr (kEpi == QI_EPI_BF16_ROWCOL) {
-              a = __fmul_rn(__fmul_rn(v[j + 2 * i], rs), p.col_scale[col0 + j + 2 * i]);
-              b = __fmul_rn(__fmul_rn(v[j + 2 * i + 1], rs), p.col_scale[col0 + j + 2 * i + 1]);
-            } else {
-              a = __fmul_rn(v[j + 2 * i], alpha);
-              b = __fmul_rn(v[j + 2 * i + 1], alpha);
-            }
-            __nv_bfloat162 h2 = __floats2bfloat162_rn(a, b);
-            w[i] = *reinterpret_cast<uint32_t*>(&h2);
-          }
-          o[j / 8] = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-      }
+      epilogue_rows<kEpi>(p, v, row, n0, half, alpha);
     }
   }
   tc_fence_before();
@@ -251,6 +228,427 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ---- block-scaled variant with scale-writer warps ----------------------------
+//
+// tcgen05.cp copies of the block scales run in the tensor pipe in series with
+// the MMAs (measured: 4 NVFP4 MMAs of a K tile 513 clk alone, 946 clk with the
+// 12 copies that feed them).  Here four warps write the scales into TMEM with
+// tcgen05.st instead (the same replicated 4 x 32-lane layout the copies
+// produce), through their own 4-stage TMEM ring, and the MMAs run without
+// interruption.  16 warps, registers rebalanced with setmaxnreg:
+//   warps 0..3   (56 regs): warp 0 TMA producer, warp 1 TMEM allocator + MMA issuer,
+//   warps 4..7   (72 regs): scale writers, one per TMEM lane quarter,
+//   warps 8..15 (192 regs): epilogue, two warps per lane quarter.
+
+constexpr int S_THREADS = 512;
+constexpr int NSF = 4;                 // TMEM scale stages
+constexpr uint32_t S_SF_COL = 256;     // stage t: columns S_SF_COL + 48t .. +48
+constexpr int S_SF_STAGE_COLS = 48;    // 16 for A (4 MMAs x 4), 32 for B (4 MMAs x 2 halves x 4)
+static_assert(S_SF_COL + NSF * S_SF_STAGE_COLS <= TMEM_COLS, "scale stages exceed TMEM");
+static_assert(56 * 128 + 72 * 128 + 192 * 256 <= 128 * S_THREADS, "register split exceeds the launch budget");
+
+QI_DEV void tmem_st16(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+template <int kEpi>
+__global__ void __launch_bounds__(S_THREADS, 1)
+    gemm_sfw_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * A_BYTES;
+  uint8_t* sSFA = sB + STAGES * B_BYTES;
+  uint8_t* sSFB = sSFA + STAGES * SFA_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sSFB + STAGES * SFB_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* sf_full = empty + STAGES;  // [NSF]
+  uint64_t* sf_empty = sf_full + NSF;  // [NSF]
+  uint64_t* acc_full = sf_empty + NSF;
+  uint64_t* acc_empty = acc_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles = p.m_tiles * p.n_tiles;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&tma_a);
+    prefetch_tensormap(&tma_b);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int t = 0; t < NSF; ++t) {
+      mbar_init(&sf_full[t], 4);  // one arrival per scale-writer warp
+      mbar_init(&sf_empty[t], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 8);  // one arrival per epilogue warp
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
+    if (warp == 0 && lane == 0) {
+      constexpr uint32_t tx = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+        const int m0 = (tile % p.m_tiles) * BM, n0 = (tile / p.m_tiles) * BN;
+        for (int kt = 0; kt < p.kt; ++kt, ++it) {
+          const int s = it % STAGES;
+          if (it >= STAGES && !(ok = mbar_wait(&empty[s], ((it / STAGES) - 1) & 1, abort_flag, p.status))) break;
+          mbar_expect_tx(&full[s], tx);
+          tma_load_2d(sA + s * A_BYTES, &tma_a, &full[s], kt * BKB, m0);
+          tma_load_2d(sB + s * B_BYTES, &tma_b, &full[s], kt * BKB, n0);
+          bulk_load(sSFA + s * SFA_BYTES, p.sfa + (int64_t)(m0 >> 7) * p.sfa_block + (int64_t)kt * 2048, 2048,
+                    &full[s]);
+          bulk_load(sSFB + s * SFB_BYTES, p.sfb + (int64_t)(n0 >> 7) * p.sfb_block + (int64_t)kt * 2048, 2048,
+                    &full[s]);
+          bulk_load(sSFB + s * SFB_BYTES + 2048, p.sfb + (int64_t)((n0 >> 7) + 1) * p.sfb_block + (int64_t)kt * 2048,
+                    2048, &full[s]);
+        }
+      }
+    } else if (warp == 1 && lane == 0) {
+      const uint32_t idesc = idesc_nvfp4(BN);
+      uint32_t it = 0, tcount = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, ++tcount) {
+        if (tcount > 0 && !(ok = mbar_wait(acc_empty, (tcount - 1) & 1, abort_flag, p.status))) break;
+        tc_fence_after();
+        for (int kt = 0; kt < p.kt; ++kt, ++it) {
+          const int s = it % STAGES, t = it % NSF;
+          if (!(ok = mbar_wait(&full[s], (it / STAGES) & 1, abort_flag, p.status))) break;
+          if (!(ok = mbar_wait(&sf_full[t], (it / NSF) & 1, abort_flag, p.status))) break;
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + s * A_BYTES), b_base = smem_u32(sB + s * B_BYTES);
+          const uint32_t sf = tmem + S_SF_COL + t * S_SF_STAGE_COLS;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_nvfp4(tmem + ACC_COL, sdesc_kmajor_sw128(a_base + kk * 32), sdesc_kmajor_sw128(b_base + kk * 32), idesc,
+                      sf + kk * 4, sf + 16 + kk * 8, (kt | kk) ? 1u : 0u);
+          tc_commit(&empty[s]);
+          tc_commit(&sf_empty[t]);
+        }
+        if (ok) tc_commit(acc_full);
+      }
+    }
+  } else if (warp < 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 72;");
+    // Scale writer for TMEM lanes [32q, 32q+32): lane l of every 512-byte
+    // atom (32 chunks of 16 bytes) goes to TMEM lane 32q + l, replicated in
+    // each quarter as the MMA reads it.  Stage layout (columns): A atoms kk at
+    // 4kk; B atoms for output columns 0..127 at 16 + 8kk, 128..255 at 20 + 8kk.
+    const int quarter = warp & 3;
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + S_SF_COL;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+      for (int kt = 0; kt < p.kt; ++kt, ++it) {
+        const int s = it % STAGES, t = it % NSF;
+        if (!(ok = mbar_wait(&full[s], (it / STAGES) & 1, abort_flag, p.status))) break;
+        if (it >= NSF && !(ok = mbar_wait(&sf_empty[t], ((it / NSF) - 1) & 1, abort_flag, p.status))) break;
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t v[S_SF_STAGE_COLS];
+        const uint4* a4 = reinterpret_cast<const uint4*>(sSFA + s * SFA_BYTES);
+        const uint4* b4 = reinterpret_cast<const uint4*>(sSFB + s * SFB_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint4 xa = a4[kk * 32 + lane], xb0 = b4[kk * 32 + lane], xb1 = b4[128 + kk * 32 + lane];
+          v[4 * kk] = xa.x, v[4 * kk + 1] = xa.y, v[4 * kk + 2] = xa.z, v[4 * kk + 3] = xa.w;
+          v[16 + 8 * kk] = xb0.x, v[17 + 8 * kk] = xb0.y, v[18 + 8 * kk] = xb0.z, v[19 + 8 * kk] = xb0.w;
+          v[20 + 8 * kk] = xb1.x, v[21 + 8 * kk] = xb1.y, v[22 + 8 * kk] = xb1.z, v[23 + 8 * kk] = xb1.w;
+        }
+        const uint32_t dst = lane_base + t * S_SF_STAGE_COLS;
+        tmem_st16(dst, v);
+        tmem_st16(dst + 16, v + 16);
+        tmem_st16(dst + 32, v + 32);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sf_full[t]);
+      }
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 192;");
+    const int quarter = warp & 3;
+    const int half = (warp - 8) >> 2;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const float alpha = p.alpha ? *p.alpha : p.alpha_value;
+    uint32_t tcount = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++tcount) {
+      const int m0 = (tile % p.m_tiles) * BM, n0 = (tile / p.m_tiles) * BN;
+      const int row = m0 + quarter * 32 + lane;
+      const bool in_range = row < p.m;
+      bool ok = mbar_wait(acc_full, tcount & 1, abort_flag, p.status);
+      ok = __all_sync(0xffffffffu, ok);
+      tc_fence_after();
+      float v[128];
+      if (ok) {
+        if constexpr (kEpi == QI_EPI_SWIGLU_NVFP4) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            tmem_ld32(tmem + lane_off + ACC_COL + half * 64 + c * 32, v + c * 32);
+            tmem_ld32(tmem + lane_off + ACC_COL + 128 + half * 64 + c * 32, v + 64 + c * 32);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_off + ACC_COL + half * 128 + c * 32, v + c * 32);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);  // the accumulator may now take the next tile
+      if (!ok) break;
+      if (!in_range) continue;
+      epilogue_rows<kEpi>(p, v, row, n0, half, alpha);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ---- paired-CTA (2-SM) variant ----------------------------------------------
+//
+// E4M3 GEMMs with two or more 128-row blocks.  A cluster of two CTAs on a TPC
+// computes 256 x 256 output tiles with cta_group::2 MMAs (M = 256): each CTA
+// stages its own 128 rows of A and its own 128 rows of B, so per SM the
+// tensor cores read half the B operand bytes of the 1-SM kernel (measured
+// about 7% faster on the O projection).  The leader (cluster rank 0) issues
+// the MMAs; both CTAs' TMA loads signal the leader's stage barrier; the
+// leader's commits arrive on both CTAs' barriers; both epilogues release the
+// accumulator to the leader.  No load uses cluster multicast.
+
+constexpr int P_STAGES = 6;
+constexpr int P_A = 128 * BKB, P_B = 128 * BKB;
+constexpr int P_STAGE = P_A + P_B;
+constexpr int P_SMEM = P_STAGES * P_STAGE + 1024 /*align*/ + 256 /*barriers*/;
+
+QI_DEV uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+QI_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Shared::cluster address of the same shared variable in CTA `rank` of the cluster.
+QI_DEV uint32_t cluster_addr(const void* local, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(local)), "r"(rank));
+  return out;
+}
+// Wait with cluster-scope acquire (arrivals may come from the peer CTA).
+QI_DEV bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+QI_DEV bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort, int* status) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t start = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((++spins & 63) == 0) {
+      if (*abort) return false;
+      if (globaltimer_ns() - start > kWaitLimitNs) {
+        *abort = 1;
+        report(status, kStatusWaitTimeout);
+        return false;
+      }
+    }
+  }
+}
+QI_DEV void mbar_arrive_remote(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+// TMA tile loads of a CTA pair: data into this CTA's shared memory, completion
+// bytes counted on the leader's barrier (cluster address).  No multicast.
+QI_DEV void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t leader_bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(map), "r"(leader_bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+QI_DEV void tmem_alloc_pair(uint32_t* smem_slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_slot)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+QI_DEV void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// Commit of the leader's MMAs arriving on the barrier at this offset in both CTAs.
+QI_DEV void tc_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+QI_DEV void mma_f8_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Instruction descriptors with M = 256 (the pair's rows).
+__host__ __device__ constexpr uint32_t with_m256(uint32_t idesc128) {
+  return (idesc128 & ~(0x1Fu << 24)) | ((uint32_t)(256 >> 4) << 24);
+}
+
+template <int kEpi>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + P_STAGES * P_A;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + P_STAGES * P_B);
+  uint64_t* empty = full + P_STAGES;
+  uint64_t* acc_full = empty + P_STAGES;
+  uint64_t* acc_empty = acc_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();  // 0: leader
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  const int m_tiles2 = (p.m + 255) / 256;
+  const int tiles = m_tiles2 * p.n_tiles;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&tma_a);
+    prefetch_tensormap(&tma_b);
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 2 * (EPI_THREADS / 32));  // one arrival per epilogue warp of both CTAs
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, TMEM_COLS);
+  tc_fence_before();
+  cluster_sync_all();  // barriers initialised and TMEM allocated in both CTAs
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t tx = 2u * (P_A + P_B);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < tiles; tile += pairs) {
+        const int m0 = (tile % m_tiles2) * 256 + (int)rank * 128, nb = (tile / m_tiles2) * BN;
+        for (int kt = 0; kt < p.kt; ++kt, ++it) {
+          const int s = it % P_STAGES;
+          if (it >= P_STAGES &&
+              !(ok = mbar_wait_cluster(&empty[s], ((it / P_STAGES) - 1) & 1, abort_flag, p.status)))
+            break;
+          const uint32_t lbar = cluster_addr(&full[s], 0);
+          if (rank == 0) mbar_expect_tx(&full[s], tx);
+          tma_load_2d_pair(sA + s * P_A, &tma_a, lbar, kt * BKB, m0);
+          tma_load_2d_pair(sB + s * P_B, &tma_b, lbar, kt * BKB, nb + (int)rank * 128);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = with_m256(idesc_e4m3(BN));
+      uint32_t it = 0, tcount = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < tiles; tile += pairs, ++tcount) {
+        if (tcount > 0 && !(ok = mbar_wait_cluster(acc_empty, (tcount - 1) & 1, abort_flag, p.status))) break;
+        tc_fence_after();
+        for (int kt = 0; kt < p.kt; ++kt, ++it) {
+          const int s = it % P_STAGES;
+          if (!(ok = mbar_wait_cluster(&full[s], (it / P_STAGES) & 1, abort_flag, p.status))) break;
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + s * P_A), b_base = smem_u32(sB + s * P_B);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_f8_pair(tmem + ACC_COL, sdesc_kmajor_sw128(a_base + kk * 32), sdesc_kmajor_sw128(b_base + kk * 32),
+                        idesc, (kt | kk) ? 1u : 0u);
+          tc_commit_pair(&empty[s]);
+        }
+        if (ok) tc_commit_pair(acc_full);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const float alpha = p.alpha ? *p.alpha : p.alpha_value;
+    const uint32_t leader_acc_empty = cluster_addr(acc_empty, 0);
+    uint32_t tcount = 0;
+    for (int tile = pair; tile < tiles; tile += pairs, ++tcount) {
+      const int m0 = (tile % m_tiles2) * 256 + (int)rank * 128, n0 = (tile / m_tiles2) * BN;
+      const int row = m0 + quarter * 32 + lane;
+      const bool in_range = row < p.m;
+      const bool ok = mbar_wait_cluster(acc_full, tcount & 1, abort_flag, p.status);
+      tc_fence_after();
+      float v[128];
+      if (ok) {
+        __syncwarp();
+        if constexpr (kEpi == QI_EPI_SWIGLU_NVFP4) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            tmem_ld32(tmem + lane_off + ACC_COL + half * 64 + c * 32, v + c * 32);
+            tmem_ld32(tmem + lane_off + ACC_COL + 128 + half * 64 + c * 32, v + 64 + c * 32);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_off + ACC_COL + half * 128 + c * 32, v + c * 32);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(leader_acc_empty);  // the accumulator may take the next tile
+      if (!ok) break;
+      if (!in_range) continue;
+      epilogue_rows<kEpi>(p, v, row, n0, half, alpha);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // neither CTA leaves while the other may still signal its barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, TMEM_COLS);
   }
 }
 
@@ -286,7 +684,7 @@ bool make_map_u8(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool kFp4, int kEpi>
+template <int kEpi>
 int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, cudaStream_t stream) {
   static bool configured[64] = {};
   int cur_dev = 0;
@@ -294,7 +692,7 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, cudaSt
   if (cur_dev < 0 || cur_dev >= 64) return (int)cudaErrorInvalidDevice;
   if (!configured[cur_dev]) {
     const cudaError_t e =
-        cudaFuncSetAttribute(gemm_kernel<kFp4, kEpi>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        cudaFuncSetAttribute(gemm_kernel<kEpi>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return (int)e;
     configured[cur_dev] = true;
   }
@@ -307,7 +705,62 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, cudaSt
   }
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = tiles < sms[cur_dev] ? tiles : sms[cur_dev];
-  gemm_kernel<kFp4, kEpi><<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, p);
+  gemm_kernel<kEpi><<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, p);
+  return (int)cudaPeekAtLastError();
+}
+
+template <int kEpi>
+int launch_sfw(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, cudaStream_t stream) {
+  static bool configured[64] = {};
+  static int sms[64] = {};
+  int cur_dev = 0;
+  cudaGetDevice(&cur_dev);
+  if (cur_dev < 0 || cur_dev >= 64) return (int)cudaErrorInvalidDevice;
+  if (!configured[cur_dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_sfw_kernel<kEpi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         SMEM_BYTES + 64);
+    if (e != cudaSuccess) return (int)e;
+    e = cudaDeviceGetAttribute(&sms[cur_dev], cudaDevAttrMultiProcessorCount, cur_dev);
+    if (e != cudaSuccess) return (int)e;
+    configured[cur_dev] = true;
+  }
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int grid = tiles < sms[cur_dev] ? tiles : sms[cur_dev];
+  gemm_sfw_kernel<kEpi><<<grid, S_THREADS, SMEM_BYTES + 64, stream>>>(ma, mb, p);
+  return (int)cudaPeekAtLastError();
+}
+
+template <int kEpi>
+int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, cudaStream_t stream) {
+  static bool configured[64] = {};
+  static int max_pairs[64] = {};
+  int cur_dev = 0;
+  cudaGetDevice(&cur_dev);
+  if (cur_dev < 0 || cur_dev >= 64) return (int)cudaErrorInvalidDevice;
+  if (!configured[cur_dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<kEpi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         P_SMEM);
+    if (e != cudaSuccess) return (int)e;
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cur_dev);
+    if (e != cudaSuccess) return (int)e;
+    // Clusters that can be resident at once (pairs of SMs on a TPC).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (sms / 2));
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = P_SMEM;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, gemm_pair_kernel<kEpi>, &cfg) != cudaSuccess ||
+        clusters < 1) {
+      cudaGetLastError();
+      clusters = sms / 2;
+    }
+    max_pairs[cur_dev] = clusters;
+    configured[cur_dev] = true;
+  }
+  const int tiles = ((p.m + 255) / 256) * p.n_tiles;
+  const int pairs = tiles < max_pairs[cur_dev] ? tiles : max_pairs[cur_dev];
+  gemm_pair_kernel<kEpi><<<2 * pairs, THREADS, P_SMEM, stream>>>(ma, mb, p);
   return (int)cudaPeekAtLastError();
 }
 
@@ -364,20 +817,34 @@ int qi_gemm(const QiGemm* g, cudaStream_t stream) {
       return (int)cudaErrorInvalidValue;
   }
   CUtensorMap ma, mb;
-  if (!make_map_u8(&ma, g->a, k_bytes, g->m, BM) || !make_map_u8(&mb, g->b, k_bytes, g->n, BN))
-    return (int)cudaErrorInvalidValue;
   if (fp4) {
+    // Block-scaled: scale factors written to TMEM by warps (see gemm_sfw_kernel).
+    if (!make_map_u8(&ma, g->a, k_bytes, g->m, BM) || !make_map_u8(&mb, g->b, k_bytes, g->n, BN))
+      return (int)cudaErrorInvalidValue;
     switch (g->epilogue) {
-      case QI_EPI_BF16: return launch<true, QI_EPI_BF16>(ma, mb, p, stream);
-      case QI_EPI_F32: return launch<true, QI_EPI_F32>(ma, mb, p, stream);
-      case QI_EPI_SWIGLU_NVFP4: return launch<true, QI_EPI_SWIGLU_NVFP4>(ma, mb, p, stream);
+      case QI_EPI_BF16: return launch_sfw<QI_EPI_BF16>(ma, mb, p, stream);
+      case QI_EPI_F32: return launch_sfw<QI_EPI_F32>(ma, mb, p, stream);
+      case QI_EPI_SWIGLU_NVFP4: return launch_sfw<QI_EPI_SWIGLU_NVFP4>(ma, mb, p, stream);
       default: return (int)cudaErrorInvalidValue;
     }
   }
+  // E4M3.  Two or more 128-row blocks: paired CTAs (2-SM MMA, 256 x 256 tiles).
+  if (g->m > BM) {
+    if (!make_map_u8(&ma, g->a, k_bytes, g->m, 128) || !make_map_u8(&mb, g->b, k_bytes, g->n, 128))
+      return (int)cudaErrorInvalidValue;
+    switch (g->epilogue) {
+      case QI_EPI_BF16: return launch_pair<QI_EPI_BF16>(ma, mb, p, stream);
+      case QI_EPI_F32: return launch_pair<QI_EPI_F32>(ma, mb, p, stream);
+      case QI_EPI_BF16_ROWCOL: return launch_pair<QI_EPI_BF16_ROWCOL>(ma, mb, p, stream);
+      default: return (int)cudaErrorInvalidValue;
+    }
+  }
+  if (!make_map_u8(&ma, g->a, k_bytes, g->m, BM) || !make_map_u8(&mb, g->b, k_bytes, g->n, BN))
+    return (int)cudaErrorInvalidValue;
   switch (g->epilogue) {
-    case QI_EPI_BF16: return launch<false, QI_EPI_BF16>(ma, mb, p, stream);
-    case QI_EPI_F32: return launch<false, QI_EPI_F32>(ma, mb, p, stream);
-    case QI_EPI_BF16_ROWCOL: return launch<false, QI_EPI_BF16_ROWCOL>(ma, mb, p, stream);
+    case QI_EPI_BF16: return launch<QI_EPI_BF16>(ma, mb, p, stream);
+    case QI_EPI_F32: return launch<QI_EPI_F32>(ma, mb, p, stream);
+    case QI_EPI_BF16_ROWCOL: return launch<QI_EPI_BF16_ROWCOL>(ma, mb, p, stream);
     default: return (int)cudaErrorInvalidValue;
   }
 }
@@ -385,11 +852,11 @@ int qi_gemm(const QiGemm* g, cudaStream_t stream) {
 int qi_gemm_resources(int* out) {
   if (!out) return (int)cudaErrorInvalidValue;
   cudaFuncAttributes a{};
-  const cudaError_t e = cudaFuncGetAttributes(&a, gemm_kernel<true, QI_EPI_BF16>);
+  const cudaError_t e = cudaFuncGetAttributes(&a, gemm_sfw_kernel<QI_EPI_BF16>);
   if (e != cudaSuccess) return (int)e;
-  out[0] = SMEM_BYTES;
+  out[0] = SMEM_BYTES + 64;
   out[1] = a.numRegs;
-  out[2] = THREADS;
+  out[2] = S_THREADS;
   return 0;
 }
 
