@@ -96,6 +96,16 @@ typedef struct QiFront {
 int qi_qk_rope_kv_append(const QiFront* p, cudaStream_t stream);
 int qi_qk_rope_kv_append_resources(int* out);
 
+/* ---- SiLU-and-mul + NVFP4 of the gate_up GEMM output -------------------
+ * Replaces the reference's act_fn + scaled_fp4_quant(is_sf_swizzled_layout=True)
+ * after gate_up_proj (src/qwen_infra/producer.py:200-206).  gate_up: bf16
+ * [rows, 2*inter] (row stride gu_row elements) as written by qi_gemm with the
+ * gate/up weight rows interleaved in 128-row blocks; out: codes [rows, inter/2]
+ * (row stride q_row bytes) and swizzled scales (128 x 4 layout) of K = inter.
+ * act = bf16(silu(gate) * up); scale = e4m3(min(amax*g/6, 448)). */
+int qi_swiglu_nvfp4(const void* gate_up, int64_t gu_row, int rows, int inter, const float* global_scale, void* q,
+                    int64_t q_row, void* scales, cudaStream_t stream);
+
 /* ---- attention output x sigmoid(gate) -> FP8 (per-token scale) --------- */
 int qi_gate_fp8(const void* out, const void* gate, int64_t out_row, int64_t gate_row, void* fp8, int64_t fp8_row,
                 float* scale, int rows, int cols, cudaStream_t stream);

@@ -279,6 +279,34 @@ __global__ void gate_fp8_kernel(const __nv_bfloat16* __restrict__ out, const __n
   reinterpret_cast<uint4*>(fp8 + row * fp8_row)[t] = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// SiLU-and-mul + NVFP4 of the gate_up GEMM output.  gu is bf16 [rows, 2I]
+// with gate and up interleaved in 128-column blocks (block b: gate channels
+// 128b.. at columns 256b.., up at 256b+128..), already bf16(acc * alpha).
+// One thread per (row, 16-channel scale group): act = bf16(silu(gate) * up),
+// then the NVFP4 quantisation with global scale g.  Grid: rows x I/16 threads
+// in blocks of 256 (high occupancy: the SiLU is ~50 exact fp32 operations per
+// element).
+__global__ void __launch_bounds__(256) swiglu_nvfp4_kernel(const __nv_bfloat16* __restrict__ gu, int64_t gu_row,
+                                                           int rows, int groups, const float* __restrict__ gscale,
+                                                           uint8_t* __restrict__ q, int64_t q_row,
+                                                           uint8_t* __restrict__ sf, int64_t gp) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)rows * groups) return;
+  const int64_t row = idx / groups;
+  const int grp = (int)(idx - row * groups);
+  const int ch = grp * 16;
+  const int64_t col = (int64_t)(ch >> 7) * 256 + (ch & 127);
+  float g[16], u[16], v[16];
+  load16_bf16(gu + row * gu_row + col, g);
+  load16_bf16(gu + row * gu_row + col + 128, u);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = bf16r(__fmul_rn(silu_f(g[j]), u[j]));
+  uint2 packed;
+  const uint32_t code = nvfp4_quant16(v, *gscale, packed);
+  *reinterpret_cast<uint2*>(q + row * q_row + (ch >> 1)) = packed;
+  sf[sf_offset(row, grp, gp)] = (uint8_t)code;
+}
+
 // Weight quantiser: fp32 [rows, K] -> NVFP4 (same arithmetic as the producer).
 __global__ void nvfp4_quant_kernel(const float* __restrict__ w, int64_t rows, int k, const float* __restrict__ g,
                                    uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
@@ -544,6 +572,22 @@ int nvfp4_attention_front_resources(int* out) {
   if (rc) return rc;
   out[0] = (int)sizeof(RefFront);
   return 0;
+}
+
+int qi_swiglu_nvfp4(const void* gate_up, int64_t gu_row, int rows, int inter, const float* global_scale, void* q,
+                    int64_t q_row, void* scales, cudaStream_t stream) {
+  QI_BIND(stream, gate_up);
+  if (rows < 1 || inter < 128 || inter % 128 || gu_row < 2 * (int64_t)inter || gu_row % 8 || q_row < inter / 2 ||
+      q_row % 8 || !gate_up || !global_scale || !q || !scales)
+    return (int)cudaErrorInvalidValue;
+  if (!aligned16(gate_up) || (reinterpret_cast<uintptr_t>(q) & 7)) return (int)cudaErrorInvalidValue;
+  const int groups = inter / 16;
+  const int64_t gp = ((int64_t)groups + 3) / 4 * 4;
+  const int64_t threads = (int64_t)rows * groups;
+  swiglu_nvfp4_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(gate_up), gu_row, rows, groups, global_scale, static_cast<uint8_t*>(q), q_row,
+      static_cast<uint8_t*>(scales), gp);
+  return (int)cudaPeekAtLastError();
 }
 
 int qi_gate_fp8(const void* out, const void* gate, int64_t out_row, int64_t gate_row, void* fp8, int64_t fp8_row,

@@ -231,6 +231,23 @@ def gemm_swiglu_nvfp4(a, sfa, b, sfb, act_global, *, m, n, k, alpha=None, alpha_
     return act_q, act_sf
 
 
+def swiglu_nvfp4(gate_up, act_global, *, act_q=None, act_sf=None):
+    """bf16 gate_up [rows, 2I] (128-column gate/up blocks) -> NVFP4 act codes
+    [rows, I/2] and swizzled scales: act = bf16(silu(gate) * up)."""
+    _cuda(gate_up, act_global)
+    rows, n = gate_up.shape
+    inter = n // 2
+    if act_q is None:
+        act_q = torch.empty((rows, inter // 2), dtype=torch.uint8, device=gate_up.device)
+    if act_sf is None:
+        act_sf = torch.empty(scale_buffer_bytes(rows, inter), dtype=torch.uint8, device=gate_up.device)
+    N.check(_run("swiglu_nvfp4", rows * (2 * n + inter // 2 + inter // 16), "B", gate_up.device,
+                 lambda: N.lib().qi_swiglu_nvfp4(_ptr(gate_up), gate_up.stride(0), rows, inter, _ptr(act_global),
+                                                 _ptr(act_q), act_q.stride(0), _ptr(act_sf),
+                                                 _stream(gate_up.device))), "qi_swiglu_nvfp4")
+    return act_q, act_sf
+
+
 def gemm_e4m3(a, b, *, m, n, k, row_scale=None, col_scale=None, alpha_value=1.0, out=None,
               out_dtype=torch.bfloat16):
     """A [m, k] E4M3 . B [n, k]^T -> bf16 scaled by row_scale[m] * col_scale[n]

@@ -250,6 +250,23 @@ def test_swiglu_epilogue_bit_exact(K, m, inter, k):
     assert np.array_equal(F.unswizzle_scales(act_sf.cpu().numpy(), m, inter), F.unswizzle_scales(sfo, m, inter))
 
 
+@pytest.mark.parametrize("rows,inter", [(1, 128), (300, 512), (2048, 1024)])
+def test_swiglu_nvfp4_kernel_bit_exact(K, rows, inter):
+    """qi_swiglu_nvfp4 on the bf16 gate_up GEMM output (128-column gate/up
+    blocks) reproduces the oracle's SiLU-and-mul + NVFP4 exactly."""
+    g = torch.Generator().manual_seed(91 + rows)
+    gu = (torch.randn(rows, 2 * inter, generator=g) * 3).to(torch.bfloat16)
+    gs = 37.5
+    act_q, act_sf = K.swiglu_nvfp4(gu.to(DEV), torch.tensor([gs], device=DEV))
+    torch.cuda.synchronize()
+    blocks = gu.float().numpy().reshape(rows, inter // 128, 2, 128)
+    gate = blocks[:, :, 0, :].reshape(rows, inter)
+    up = blocks[:, :, 1, :].reshape(rows, inter)
+    qo, sfo, _ = P.swiglu_nvfp4(gate, up, 1.0, gs)
+    assert np.array_equal(act_q.cpu().numpy(), qo)
+    assert np.array_equal(F.unswizzle_scales(act_sf.cpu().numpy(), rows, inter), F.unswizzle_scales(sfo, rows, inter))
+
+
 def _kv_fixture(K, tokens, kvh, d, seed, page_size=16):
     rng = np.random.default_rng(seed)
     pages = (tokens + page_size - 1) // page_size + 5
