@@ -5,7 +5,9 @@
 One step = one bank: R requests x L prompt tokens (default 4 x 32768) of the
 27B-shaped NVFP4 decoder, chunk 2048, through 2N virtual stages folded onto N
 GPUs (one process per GPU, launched by torchrun for N > 1).  Prints one JSON
-line on rank 0.  Inputs: seeded synthetic embeddings and random-init weights
+line on rank 0 (``--profile cpp``: the conventional N-stage pipeline on the
+same kernels and transport instead, the comparison arm for the fold's bubble).
+Inputs: seeded synthetic embeddings and random-init weights
 of the architecture (no checkpoint); the weights (~16 GB NVFP4) and KV pages
 exceed L2, so no extra flush is needed between banks.
 
@@ -45,6 +47,9 @@ def parse():
     p.add_argument("--prompt-tokens", type=int, default=32768)
     p.add_argument("--chunk-size", type=int, default=2048)
     p.add_argument("--transport", choices=("p2p", "nccl"), default="p2p")
+    p.add_argument("--profile", choices=("vpp", "cpp"), default="vpp",
+                   help="vpp: 2N virtual stages folded onto N GPUs; cpp: the conventional N-stage pipeline "
+                        "(the comparison arm)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-kernel-timing", action="store_true")
@@ -219,9 +224,11 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
         from qwen_infra_b200.vpp.stages import StageBoundaries
 
-        transport = StageBoundaries(rank, world, dev, args.chunk_size, shape.hidden, backend=args.transport)
+        transport = StageBoundaries(rank, world, dev, args.chunk_size, shape.hidden, backend=args.transport,
+                                    profile=args.profile)
     request_tokens = [args.prompt_tokens] * args.requests
-    runner = FoldedRank(shape, rank, world, dev, request_tokens, args.chunk_size, transport=transport)
+    runner = FoldedRank(shape, rank, world, dev, request_tokens, args.chunk_size, transport=transport,
+                        profile=args.profile)
     gen = torch.Generator(device=dev).manual_seed(4321)
     embeds = [torch.randn(t, shape.hidden, generator=gen, device=dev).to(torch.bfloat16) for t in request_tokens] \
         if rank == 0 else None
@@ -298,7 +305,7 @@ def run_ours(args):
         t0.record(stream)
         for _ in range(args.steps):
             last = runner.run_bank(None, host_embeds=host)
-            if rank == 0:
+            if rank == runner.output_rank:
                 out_host.copy_(last, non_blocking=True)
         t1.record(stream)
         torch.cuda.synchronize()
@@ -360,10 +367,13 @@ def run_ours(args):
         vs_baseline=None, dtype="nvfp4 (e2m1 x e4m3/16, fp32 accum), fp8 O-proj, bf16 attention",
         data="synthetic (seeded embeddings, random-init weights of the architecture)",
         config=dict(workload=f"{args.model} {args.requests}x{args.prompt_tokens} tokens, chunk {args.chunk_size}, "
-                             f"{2 * world} virtual stages on {world} GPU(s)",
+                             + (f"{2 * world} virtual stages on {world} GPU(s)" if args.profile == "vpp"
+                                else f"conventional {world}-stage pipeline"),
+                    profile=args.profile,
                     model=args.model, layers=shape.layers, requests=args.requests,
-                    prompt_tokens=args.prompt_tokens, chunk=args.chunk_size, virtual_stages=2 * world,
-                    parallelism=f"folded-vpp pp{world}", transport=(args.transport if world > 1 else "local fold"),
+                    prompt_tokens=args.prompt_tokens, chunk=args.chunk_size,
+                    virtual_stages=2 * world if args.profile == "vpp" else world,
+                    parallelism=f"folded-vpp pp{world}" if args.profile == "vpp" else f"pp{world}", transport=(args.transport if world > 1 else "local fold"),
                     l2="inputs larger than L2 (weights ~16 GB, KV pages)"),
         bubble_fraction=bubble, busiest_rank_compute_ms=busiest, instrumented_bank_ms=makespan,
         model_tflops=total_flops / (ms / 1e3) / 1e12,

@@ -8,7 +8,8 @@ Models are synthetic (seeded NVFP4 weights of a named shape: ``qwen27b`` or
 ``tiny``), prompts are seeded embeddings of ``--prompt-tokens`` tokens.
 ``--transport segment-dma`` selects the peer-to-peer copy-engine transport
 (the reference's segmented DMA edge, rebuilt for NVLink); ``nccl`` the NCCL
-send/recv comparison.  ``--profile cpp`` is not built yet and is rejected.
+send/recv comparison.  ``--profile cpp`` runs the conventional G-stage
+pipeline on the same kernels and transport (the comparison arm for the fold).
 Output: one JSON record per request with the final-normed hidden state of
 its last prompt token (norm and a digest), printed as a JSON list.
 """
@@ -83,15 +84,14 @@ def _prefill(args):
         print(json.dumps(dict(engine=options, requests=args.requests, prompt_tokens=args.prompt_tokens,
                               gpus=args.gpus), indent=2))
         return 0
-    if args.profile != "vpp":
-        raise ValueError("only the folded VPP profile is built in this repository")
     from .vpp.launch import BankJob, launch
 
     import torch
 
     gpus = args.gpus or min(4, torch.cuda.device_count())
     job = BankJob(model=args.model, requests=args.requests, prompt_tokens=args.prompt_tokens,
-                  chunk=args.chunk_size, transport="p2p" if args.transport == "segment-dma" else "nccl")
+                  chunk=args.chunk_size, transport="p2p" if args.transport == "segment-dma" else "nccl",
+                  profile=args.profile)
     with tempfile.TemporaryDirectory() as tmp:
         result = launch(job, gpus, Path(tmp) / "bank.pt")
     print(json.dumps(_records(result["outputs"], args.requests), indent=2))
@@ -101,7 +101,7 @@ def _prefill(args):
 def main(argv=None):
     parser = argparse.ArgumentParser(prog="qwen-infra")
     sub = parser.add_subparsers(dest="command", required=True)
-    prefill = sub.add_parser("prefill", help="Run a bounded folded-VPP prefill bank")
+    prefill = sub.add_parser("prefill", help="Run a bounded prefill bank (folded VPP or conventional pipeline)")
     prefill.add_argument("--model", required=True, choices=("qwen27b", "tiny"))
     prefill.add_argument("--profile", choices=PREFILL_PROFILES, default="vpp")
     prefill.add_argument("--transport", choices=("segment-dma", "nccl"), default="segment-dma")

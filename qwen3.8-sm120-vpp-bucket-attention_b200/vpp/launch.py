@@ -1,6 +1,7 @@
 """Launch one bank on G GPUs: one worker process per GPU (spawned here, or
 started by torchrun), NCCL process group for the device plumbing, gloo for
-the boundary control plane, 2G virtual stages folded onto the G ranks.
+the boundary control plane, 2G virtual stages folded onto the G ranks (or,
+with ``profile="cpp"``, the conventional G-stage pipeline).
 """
 
 import os
@@ -21,6 +22,7 @@ class BankJob:
     prompt_tokens: int = 8192
     chunk: int = 2048
     transport: str = "p2p"  # or "nccl"
+    profile: str = "vpp"  # or "cpp" (conventional pipeline, the comparison arm)
     seed: int = 4321
     keep_all_outputs: bool = False
     banks: int = 1
@@ -48,7 +50,8 @@ def seeded_embeddings(job, hidden, device):
 
 
 def run_rank(job, rank, world, local_rank):
-    """Body of one rank; returns rank 0's outputs (CPU tensors) or None."""
+    """Body of one rank; returns the output rank's outputs (CPU tensors; rank 0
+    folded, rank G-1 conventional) or None, and the transport receipt."""
     from .runner import FoldedRank
     from .stages import StageBoundaries
 
@@ -58,17 +61,17 @@ def run_rank(job, rank, world, local_rank):
     transport = None
     if world > 1:
         transport = StageBoundaries(rank, world, dev, job.chunk, shape.hidden, backend=job.transport,
-                                    timeout=job.timeout_s)
+                                    timeout=job.timeout_s, profile=job.profile)
     runner = FoldedRank(shape, rank, world, dev, job.tokens(), job.chunk, transport=transport,
                         keep_all_outputs=job.keep_all_outputs,
-                        on_device_init=shape.hidden > 2048)
+                        on_device_init=shape.hidden > 2048, profile=job.profile)
     embeds = seeded_embeddings(job, shape.hidden, dev) if rank == 0 else None
     out = None
     for _ in range(job.banks):
         last = runner.run_bank(embeds)
     torch.cuda.synchronize(dev)
     runner.model.check_status()
-    if rank == 0:
+    if rank == runner.output_rank:
         if job.keep_all_outputs:
             out = {b: t.float().cpu() for b, t in runner.outputs.items()}
         else:
@@ -93,15 +96,15 @@ def _worker(rank, world, port, job_dict, result_path):
                             timeout=timedelta(seconds=job.timeout_s))
     try:
         out, receipt = run_rank(job, rank, world, rank)
-        if rank == 0:
+        if rank == (world - 1 if job.profile == "cpp" else 0):  # the output rank writes the result
             torch.save(dict(outputs=out, receipt=receipt), result_path)
     finally:
         dist.destroy_process_group()
 
 
 def launch(job, world, result_path):
-    """Spawn ``world`` workers (GPU i for rank i) and run the bank(s); rank 0
-    writes its outputs to ``result_path``; returns what it wrote."""
+    """Spawn ``world`` workers (GPU i for rank i) and run the bank(s); the
+    output rank writes its outputs to ``result_path``; returns what it wrote."""
     if world > torch.cuda.device_count():
         raise ValueError(f"{world} ranks but {torch.cuda.device_count()} visible GPUs")
     import __graft_entry__

@@ -180,6 +180,39 @@ def rank_local_stage_orders(batch_ids, ranks=4):
     return orders
 
 
+# ---------------------------------------------------------------------------
+# Conventional pipeline (the reference's ``--profile cpp``: vLLM pipeline
+# parallel with G stages, ``src/qwen_infra/config.py:74-80``), kept as the
+# comparison arm for the fold: G stages of L/G layers, stage r on rank r,
+# every chunk crossing ranks 0 -> 1 -> ... -> G-1, the last rank producing the
+# output.  Its boundaries are the forward wire edges of the folded layout
+# (stage s -> s+1 for s < G-1), so the same transport carries them.
+# ---------------------------------------------------------------------------
+
+PROFILES = ("vpp", "cpp")
+
+
+def cpp_layer_range(rank, ranks=4, layers=64):
+    """Layer span of ``rank``'s single stage in the conventional pipeline."""
+    _check_rank(rank, ranks)
+    per = layers // ranks
+    if per * ranks != layers:
+        raise ValueError("Layers must split evenly into G stages")
+    return rank * per, (rank + 1) * per
+
+
+def cpp_stage_orders(batch_ids, ranks=4):
+    """Each rank's [(batch, stage)] list in the conventional pipeline: every
+    batch through the rank's one stage, in admission order (per-stage FIFO,
+    which keeps each layer's KV history in chunk order)."""
+    bank = tuple(batch_ids)
+    if not bank or len(bank) > 65536:
+        raise ValueError("Expected one bounded nonempty bank")
+    if type(ranks) is not int or ranks < 1:
+        raise ValueError("Expected a positive number of ranks")
+    return [[(b, r) for b in bank] for r in range(ranks)]
+
+
 def retained_boundary_bytes(tokens, live_batches=6, hidden=5120):
     """Bytes of dual-bf16 boundary planes kept for ``live_batches`` messages."""
     if tokens <= 0 or not 1 <= live_batches <= 6:

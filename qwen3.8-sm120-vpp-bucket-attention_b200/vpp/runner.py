@@ -11,6 +11,10 @@ the same order the reference's executor messages produce,
 
 Per-stage FIFO order makes the KV history of chunk j+1 ready when it reaches
 a layer: chunk j passed the same stage, on the same stream, before it.
+
+``profile="cpp"`` runs the conventional pipeline instead (the reference's
+``--profile cpp``): one stage of L/G layers per rank, chunks in order through
+ranks 0..G-1, output on rank G-1 -- the comparison arm for the fold's bubble.
 """
 
 from dataclasses import dataclass
@@ -38,21 +42,33 @@ def plan_bank(request_tokens, chunk):
 
 
 class FoldedRank:
-    """Rank ``rank`` of ``ranks``: owns stages rank and 2G-1-rank."""
+    """Rank ``rank`` of ``ranks``.  Folded (``profile="vpp"``): owns stages
+    rank and 2G-1-rank, output on rank 0.  Conventional (``"cpp"``): owns
+    stage rank of G, output on rank G-1."""
 
     def __init__(self, shape, rank, ranks, device, request_tokens, chunk, *, transport=None, base_seed=1234,
-                 on_device_init=None, keep_all_outputs=False):
-        self.shape, self.rank, self.ranks = shape, rank, ranks
+                 on_device_init=None, keep_all_outputs=False, profile="vpp"):
+        if profile not in L.PROFILES:
+            raise ValueError("profile is vpp or cpp")
+        self.shape, self.rank, self.ranks, self.profile = shape, rank, ranks, profile
         self.device = torch.device(device)
         self.request_tokens = list(request_tokens)
         self.chunk = chunk
-        self.spans = L.layer_ranges(rank, ranks, shape.layers)
-        layers = list(range(*self.spans[0])) + list(range(*self.spans[1]))
-        self.model = StageModel(shape, layers, self.device, max_rows=chunk, request_tokens=self.request_tokens,
-                                base_seed=base_seed, on_device_init=on_device_init, final_norm=(rank == 0))
-        self.transport = transport
         self.chunks = plan_bank(self.request_tokens, chunk)
-        self.order = L.rank_local_stage_orders([c.batch for c in self.chunks], ranks)[rank]
+        batches = [c.batch for c in self.chunks]
+        if profile == "vpp":
+            self.spans = L.layer_ranges(rank, ranks, shape.layers)
+            self.stage_count, self.output_rank = 2 * ranks, 0
+            self.order = L.rank_local_stage_orders(batches, ranks)[rank]
+        else:
+            self.spans = (L.cpp_layer_range(rank, ranks, shape.layers),)
+            self.stage_count, self.output_rank = ranks, ranks - 1
+            self.order = L.cpp_stage_orders(batches, ranks)[rank]
+        layers = [layer for span in self.spans for layer in range(*span)]
+        self.model = StageModel(shape, layers, self.device, max_rows=chunk, request_tokens=self.request_tokens,
+                                base_seed=base_seed, on_device_init=on_device_init,
+                                final_norm=(rank == self.output_rank))
+        self.transport = transport
         self.keep_all_outputs = keep_all_outputs
         h = shape.hidden
         self.fold = (torch.empty((chunk, h), dtype=torch.bfloat16, device=self.device),
@@ -72,7 +88,8 @@ class FoldedRank:
         per request (list), or None with ``host_embeds`` (pinned host tensors,
         copied chunk by chunk inside the run)."""
         G = self.ranks
-        last_stage = 2 * G - 1
+        last_stage = self.stage_count - 1
+        folded = self.profile == "vpp"
         ctxs = self._contexts()
         stream = torch.cuda.current_stream(self.device)
         self.stage_events = []
@@ -87,16 +104,17 @@ class FoldedRank:
                 else:
                     hidden = embeds[ch.request][ch.start:ch.start + ch.rows]
                 residual = None
-            elif stage == G:  # local fold: stage G-1 ran on this rank just before
+            elif folded and stage == G:  # local fold: stage G-1 ran on this rank just before
                 hidden, residual = self.fold[0][:ch.rows], self.fold[1][:ch.rows]
             else:
                 hidden, residual = self.transport.receive(batch, stage, ch.rows)
             if record_events:  # after the input is ready: stage time excludes waiting
                 ev0 = torch.cuda.Event(enable_timing=True)
                 ev0.record(stream)
-            span = L.stage_layers(stage, G, self.shape.layers)
+            span = (L.stage_layers(stage, G, self.shape.layers) if folded
+                    else L.cpp_layer_range(stage, G, self.shape.layers))
             on_residual = None
-            if stage == G - 1:
+            if folded and stage == G - 1:
                 out_planes = (self.fold[0][:ch.rows], self.fold[1][:ch.rows])
             elif stage == last_stage:
                 out_planes = None
@@ -104,9 +122,9 @@ class FoldedRank:
                 out_planes = self.transport.prepare_send(batch, stage, ch.rows)
                 on_residual = (lambda b=batch, s=stage: self.transport.mark_residual_ready(b, s))
             h, r = self.model.run_layers(span, hidden, residual, ctx, out_planes, on_residual)
-            if stage not in (G - 1, last_stage):
+            if stage != last_stage and not (folded and stage == G - 1):
                 self.transport.send(batch, stage, ch.rows)
-            if stage not in (0, G):
+            if stage != 0 and not (folded and stage == G):
                 self.transport.retire(batch, stage)
             if stage == last_stage:
                 if self.keep_all_outputs:

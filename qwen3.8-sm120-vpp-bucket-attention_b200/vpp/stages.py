@@ -48,13 +48,31 @@ class _Edge:
         self.forward = src_stage < ranks - 1
 
 
+def boundary_edges(rank, ranks, profile="vpp"):
+    """({stage: edge out of it}, {stage: edge into it}) for this rank's stages.
+    Folded: stages rank and 2G-1-rank, every boundary but the fold is a wire
+    edge.  Conventional: stage rank only, edges s -> s+1 for s < G-1 (the
+    forward edges of the folded layout, same indices and rings)."""
+    if profile == "vpp":
+        stages, n_stages = (rank, 2 * ranks - 1 - rank), 2 * ranks
+    elif profile == "cpp":
+        stages, n_stages = (rank,), ranks
+    else:
+        raise ValueError("profile is vpp or cpp")
+    out_edges = {s: _Edge(s, ranks) for s in stages if s + 1 < n_stages and L.stage_rank(s + 1, ranks) != rank}
+    in_edges = {s: _Edge(s - 1, ranks) for s in stages if s > 0 and L.stage_rank(s - 1, ranks) != rank}
+    return out_edges, in_edges
+
+
 class StageBoundaries:
     def __init__(self, rank, ranks, device, capacity, hidden, *, backend="p2p", epoch=1, timeout=60.0,
-                 segment_bytes=16 << 20, control_group=None, session=None):
+                 segment_bytes=16 << 20, control_group=None, session=None, profile="vpp"):
         if ranks < 2:
             raise ValueError("a boundary transport needs at least two ranks")
         if backend not in ("p2p", "nccl"):
             raise ValueError("backend is p2p or nccl")
+        if profile not in L.PROFILES:
+            raise ValueError("profile is vpp or cpp")
         self.rank, self.ranks, self.backend = rank, ranks, backend
         self.device = torch.device(device)
         self.dev_index = self.device.index
@@ -66,9 +84,7 @@ class StageBoundaries:
         self.slot_bytes = 2 * self.plane_bytes
         self.closed = self.failed = False
         self.group = control_group or dist.new_group(backend="gloo")
-        stages = (rank, 2 * ranks - 1 - rank)
-        self.out_edges = {s: _Edge(s, ranks) for s in stages if s + 1 < 2 * ranks and L.stage_rank(s + 1, ranks) != rank}
-        self.in_edges = {s: _Edge(s - 1, ranks) for s in stages if s > 0 and L.stage_rank(s - 1, ranks) != rank}
+        self.out_edges, self.in_edges = boundary_edges(rank, ranks, profile)
         # logical rings per edge (source side for outgoing, destination side for incoming)
         self.src_rings = {s: NV.SlotRing(NV.SOURCE, self.layout, epoch, e.src_stage) for s, e in self.out_edges.items()}
         self.dst_rings = {s: NV.SlotRing(NV.DESTINATION, self.layout, epoch, e.src_stage)

@@ -108,3 +108,41 @@ def test_profile_annotation():
     assert body["stage"] == 6 and body["layers"] == [48, 56]
     with pytest.raises(ValueError):
         L.profile_annotation(1, 2, 7, "compute", [])
+
+
+# --- conventional pipeline (the comparison arm) ------------------------------
+
+@pytest.mark.parametrize("ranks", [1, 2, 4, 8])
+def test_cpp_ranges_cover_each_layer_once_in_order(ranks):
+    spans = [L.cpp_layer_range(r, ranks, 64) for r in range(ranks)]
+    assert [i for lo, hi in spans for i in range(lo, hi)] == list(range(64))
+    with pytest.raises(ValueError):
+        L.cpp_layer_range(0, 3, 64)  # 64 layers do not split into 3 stages
+
+
+@pytest.mark.parametrize("ranks", [1, 2, 4, 8])
+def test_cpp_orders_are_per_stage_fifo(ranks):
+    bank = list(range(11))
+    orders = L.cpp_stage_orders(bank, ranks)
+    assert len(orders) == ranks
+    for r, order in enumerate(orders):
+        assert order == [(b, r) for b in bank]
+    with pytest.raises(ValueError):
+        L.cpp_stage_orders([], ranks)
+
+
+@pytest.mark.parametrize("ranks", [2, 4, 8])
+def test_cpp_boundaries_are_the_forward_wire_edges(ranks):
+    from qwen_infra_b200.vpp.stages import boundary_edges
+
+    for r in range(ranks):
+        out_e, in_e = boundary_edges(r, ranks, "cpp")
+        assert sorted(out_e) == ([r] if r < ranks - 1 else [])
+        assert sorted(in_e) == ([r] if r > 0 else [])
+        for s, e in out_e.items():
+            assert (e.src_rank, e.dst_rank, e.forward) == (r, r + 1, True)
+            # same edge index as the folded layout's forward edge out of stage s
+            assert e.index == boundary_edges(r, ranks, "vpp")[0][s].index
+    # folded edges are unchanged: every source stage but the fold and the last
+    srcs = sorted(s for r in range(ranks) for s in boundary_edges(r, ranks, "vpp")[0])
+    assert tuple(srcs) == L.wire_edges(ranks)
