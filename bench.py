@@ -215,8 +215,9 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     shape = M.SHAPES[args.model]
     if args.layers:
-        shape = M.ModelShape(args.layers, shape.hidden, shape.qheads, shape.kvheads, shape.head_dim,
-                             shape.intermediate)
+        from dataclasses import replace
+
+        shape = replace(shape, layers=args.layers)
     transport = None
     if world > 1:
         from datetime import timedelta
@@ -296,7 +297,7 @@ def run_ours(args):
     e2e = None
     if not args.no_e2e:
         host = [e.cpu().pin_memory() for e in embeds] if rank == 0 else None
-        out_host = torch.empty((args.requests, shape.hidden), dtype=torch.bfloat16).pin_memory()
+        out_host = torch.empty(args.requests, dtype=torch.int32).pin_memory()  # the output token ids
         runner.run_bank(None, host_embeds=host)
         torch.cuda.synchronize()
         barrier()
@@ -304,16 +305,16 @@ def run_ours(args):
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record(stream)
         for _ in range(args.steps):
-            last = runner.run_bank(None, host_embeds=host)
+            runner.run_bank(None, host_embeds=host)
             if rank == runner.output_rank:
-                out_host.copy_(last, non_blocking=True)
+                out_host.copy_(runner.last_tokens, non_blocking=True)
         t1.record(stream)
         torch.cuda.synchronize()
         barrier()
         e2e_ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
         tokens = args.requests * args.prompt_tokens
         e2e = dict(value=tokens / (e2e_ms / 1e3), unit="tok/s", ms_per_step=e2e_ms,
-                   h2d_bytes_per_step=tokens * shape.hidden * 2, d2h_bytes_per_step=args.requests * shape.hidden * 2)
+                   h2d_bytes_per_step=tokens * shape.hidden * 2, d2h_bytes_per_step=args.requests * 4)
 
     if rank != 0:
         if transport is not None:

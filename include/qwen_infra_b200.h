@@ -106,6 +106,20 @@ int qi_qk_rope_kv_append_resources(int* out);
 int qi_swiglu_nvfp4(const void* gate_up, int64_t gu_row, int rows, int inter, const float* global_scale, void* q,
                     int64_t q_row, void* scales, cudaStream_t stream);
 
+/* ---- LM head + greedy sampling of the output token ----------------------
+ * Replaces the reference's LM head and temperature-0 sampling of the one
+ * output token (src/qwen_infra/cli.py:145; logical rank 0, vpp/runner.py:324-352).
+ * hidden: bf16 [rows, dim] final-normed (row stride hidden_row elements);
+ * weight: bf16 [vocab, dim]; logits: optional fp32 [rows, vocab] (NULL: not
+ * written); tokens: int32 [rows], argmax with the lowest index on ties (-1 if
+ * every logit is NaN).  rows <= 8, dim % 8 == 0, dim <= 8192.  workspace:
+ * qi_lm_head_workspace_bytes() bytes, 8-byte aligned, zero-filled before the
+ * first call and left zero by every call; calls that overlap on the GPU need
+ * separate workspaces. */
+int qi_lm_head_argmax(const void* hidden, int64_t hidden_row, int rows, int dim, const void* weight, int vocab,
+                      float* logits, void* workspace, int* tokens, cudaStream_t stream);
+int qi_lm_head_workspace_bytes(void);
+
 /* ---- attention output x sigmoid(gate) -> FP8 (per-token scale) --------- */
 int qi_gate_fp8(const void* out, const void* gate, int64_t out_row, int64_t gate_row, void* fp8, int64_t fp8_row,
                 float* scale, int rows, int cols, cudaStream_t stream);

@@ -297,3 +297,38 @@ def quantize_weight_fp8_rows(w):
     amax = np.abs(w).max(axis=1).astype(f32)
     scale = np.maximum((amax / f32(448.0)).astype(f32), f32(np.finfo(np.float32).tiny)).astype(f32)
     return F.e4m3_encode((w / scale[:, None]).astype(f32)), scale
+
+
+def lm_head_argmax(hidden, weight):
+    """Greedy sampling of the output token (the reference samples with
+    temperature 0: src/qwen_infra/cli.py:145): logits[r, v] = <hidden[r], W[v]>
+    with the kernel's fp32 order -- lane l of a warp sums the 8-element chunks
+    l, l+32, ... of the row in order (one rounded multiply and one rounded add
+    per element), then the 32 lane sums are combined by the xor butterfly --
+    and token[r] = argmax_v, lowest index on ties, NaN never chosen.
+    hidden [R, H], weight [V, H]: float32 arrays holding bf16 values.
+    Returns (logits [R, V] float32, tokens [R] int)."""
+    h = np.asarray(hidden, dtype=f32)
+    w = np.asarray(weight, dtype=f32)
+    rows, dim = h.shape
+    vocab = w.shape[0]
+    chunks = dim // 8
+    acc = np.zeros((rows, vocab, 32), dtype=f32)
+    for step in range((chunks + 31) // 32):
+        lanes = np.arange(32)
+        c = lanes + 32 * step
+        live = c < chunks
+        c = np.minimum(c, chunks - 1)
+        for e in range(8):
+            col = c * 8 + e  # [32]
+            prod = (w[None, :, col] * h[:, None, col]).astype(f32)  # [R, V, 32]
+            acc = np.where(live[None, None, :], (acc + prod).astype(f32), acc)
+    logits = butterfly_sum(acc)
+    bits = logits.view(np.uint32)
+    ordv = np.where(bits & np.uint32(0x80000000), ~bits, bits | np.uint32(0x80000000)).astype(np.uint64)
+    idx = np.arange(vocab, dtype=np.uint64)
+    keys = (ordv << np.uint64(32)) | (np.uint64(0xFFFFFFFF) - idx)[None, :]
+    keys = np.where(np.isnan(logits), np.uint64(0), keys)
+    best = keys.max(axis=1)
+    tokens = np.where(best == 0, -1, (np.uint64(0xFFFFFFFF) - (best & np.uint64(0xFFFFFFFF))).astype(np.int64))
+    return logits, tokens.astype(np.int64)

@@ -10,8 +10,10 @@ Models are synthetic (seeded NVFP4 weights of a named shape: ``qwen27b`` or
 (the reference's segmented DMA edge, rebuilt for NVLink); ``nccl`` the NCCL
 send/recv comparison.  ``--profile cpp`` runs the conventional G-stage
 pipeline on the same kernels and transport (the comparison arm for the fold).
-Output: one JSON record per request with the final-normed hidden state of
-its last prompt token (norm and a digest), printed as a JSON list.
+Output: the reference's record per request (``request_id``, ``text``,
+``token_ids`` = the greedy output token, ``finished``), printed as a JSON list;
+``text`` is empty (the synthetic model has no tokenizer), and each record adds
+the norm and a digest of the final-normed hidden state it was sampled from.
 """
 
 import argparse
@@ -62,11 +64,11 @@ class PrefillConfig:
         return options
 
 
-def _records(outputs, requests):
+def _records(outputs, requests, tokens):
     recs = []
     for r in range(requests):
         v = outputs[r]
-        recs.append(dict(request_id=str(r), finished=True, token_ids=[],
+        recs.append(dict(request_id=str(r), text="", token_ids=[int(tokens[r])], finished=True,
                          final_hidden_norm=float(v.norm()),
                          final_hidden_sha256=hashlib.sha256(v.to("cpu").numpy().tobytes()).hexdigest()[:16]))
     return recs
@@ -94,7 +96,7 @@ def _prefill(args):
                   profile=args.profile)
     with tempfile.TemporaryDirectory() as tmp:
         result = launch(job, gpus, Path(tmp) / "bank.pt")
-    print(json.dumps(_records(result["outputs"], args.requests), indent=2))
+    print(json.dumps(_records(result["outputs"], args.requests, result["tokens"]), indent=2))
     return 0
 
 

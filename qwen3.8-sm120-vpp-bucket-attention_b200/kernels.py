@@ -248,6 +248,31 @@ def swiglu_nvfp4(gate_up, act_global, *, act_q=None, act_sf=None):
     return act_q, act_sf
 
 
+_LM_WORKSPACE = {}
+
+
+def lm_head_argmax(hidden, weight, *, tokens=None, logits=None):
+    """Greedy output token per row: argmax_v <hidden[r], weight[v]> (bf16
+    inputs, fp32 logits, lowest index on ties).  ``logits``: optional fp32
+    [rows, vocab] to receive the logits.  Returns int32 tokens [rows]."""
+    _cuda(hidden, weight)
+    rows, dim = hidden.shape
+    vocab = weight.shape[0]
+    dev = hidden.device
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    ws = _LM_WORKSPACE.get(key)
+    if ws is None:
+        ws = torch.zeros(N.lib().qi_lm_head_workspace_bytes(), dtype=torch.uint8, device=dev)
+        _LM_WORKSPACE[key] = ws
+    if tokens is None:
+        tokens = torch.empty(rows, dtype=torch.int32, device=dev)
+    N.check(_run("lm_head", vocab * dim * 2 + rows * dim * 2, "B", dev,
+                 lambda: N.lib().qi_lm_head_argmax(_ptr(hidden), hidden.stride(0), rows, dim, _ptr(weight), vocab,
+                                                   _ptr(logits), _ptr(ws), _ptr(tokens), _stream(dev))),
+            "qi_lm_head_argmax")
+    return tokens
+
+
 def gemm_e4m3(a, b, *, m, n, k, row_scale=None, col_scale=None, alpha_value=1.0, out=None,
               out_dtype=torch.bfloat16):
     """A [m, k] E4M3 . B [n, k]^T -> bf16 scaled by row_scale[m] * col_scale[n]

@@ -34,11 +34,13 @@ class BankJob:
 
 
 def shape_of(job):
-    from .model import SHAPES, ModelShape
+    from dataclasses import replace
+
+    from .model import SHAPES
 
     s = SHAPES[job.model]
     if job.layers and job.layers != s.layers:
-        s = ModelShape(job.layers, s.hidden, s.qheads, s.kvheads, s.head_dim, s.intermediate)
+        s = replace(s, layers=job.layers)
     return s
 
 
@@ -51,7 +53,8 @@ def seeded_embeddings(job, hidden, device):
 
 def run_rank(job, rank, world, local_rank):
     """Body of one rank; returns the output rank's outputs (CPU tensors; rank 0
-    folded, rank G-1 conventional) or None, and the transport receipt."""
+    folded, rank G-1 conventional) or None, the transport receipt, and the
+    output rank's sampled token per request (or None)."""
     from .runner import FoldedRank
     from .stages import StageBoundaries
 
@@ -66,7 +69,7 @@ def run_rank(job, rank, world, local_rank):
                         keep_all_outputs=job.keep_all_outputs,
                         on_device_init=shape.hidden > 2048, profile=job.profile)
     embeds = seeded_embeddings(job, shape.hidden, dev) if rank == 0 else None
-    out = None
+    out = tokens = None
     for _ in range(job.banks):
         last = runner.run_bank(embeds)
     torch.cuda.synchronize(dev)
@@ -76,8 +79,9 @@ def run_rank(job, rank, world, local_rank):
             out = {b: t.float().cpu() for b, t in runner.outputs.items()}
         else:
             out = last.float().cpu()
+        tokens = runner.last_tokens.cpu().tolist()
     receipt = transport.close() if transport is not None else None
-    return out, receipt
+    return out, receipt, tokens
 
 
 def _free_port():
@@ -95,9 +99,9 @@ def _worker(rank, world, port, job_dict, result_path):
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                             timeout=timedelta(seconds=job.timeout_s))
     try:
-        out, receipt = run_rank(job, rank, world, rank)
+        out, receipt, tokens = run_rank(job, rank, world, rank)
         if rank == (world - 1 if job.profile == "cpp" else 0):  # the output rank writes the result
-            torch.save(dict(outputs=out, receipt=receipt), result_path)
+            torch.save(dict(outputs=out, receipt=receipt, tokens=tokens), result_path)
     finally:
         dist.destroy_process_group()
 

@@ -33,6 +33,7 @@ class ModelShape:
     eps: float = 1e-6
     rope_theta: float = 1e6
     page_size: int = 16
+    vocab: int = 152064  # LM head rows (the Qwen embedding size)
 
     @property
     def qkv_out(self):
@@ -48,7 +49,7 @@ class ModelShape:
         return 4 * self.qheads * self.head_dim * pairs
 
 
-TINY = ModelShape(layers=4, hidden=1024, qheads=16, kvheads=4, head_dim=64, intermediate=3072)
+TINY = ModelShape(layers=4, hidden=1024, qheads=16, kvheads=4, head_dim=64, intermediate=3072, vocab=4096)
 QWEN27B = ModelShape(layers=64, hidden=5120, qheads=64, kvheads=8, head_dim=128, intermediate=17408)
 SHAPES = {"tiny": TINY, "qwen27b": QWEN27B}
 
@@ -59,6 +60,7 @@ ACT_GLOBAL_DOWN = float(np.float32(2688.0 / 64.0))
 KV_GLOBAL_K = float(np.float32(16.0 / 2688.0))
 KV_GLOBAL_V = float(np.float32(8.0 / 2688.0))
 FINAL_NORM_SEED_OFFSET = 999_983
+LM_HEAD_SEED_OFFSET = 999_979
 
 
 def _seeded_normal(shape, seed, std, device, on_device):
@@ -203,10 +205,12 @@ class StageModel:
         f = lambda v: torch.tensor([v], dtype=torch.float32, device=self.device)
         self.g_norm, self.g_down = f(ACT_GLOBAL_NORM), f(ACT_GLOBAL_DOWN)
         self.kg, self.vg = f(KV_GLOBAL_K), f(KV_GLOBAL_V)
-        self.final_gamma = None
-        if final_norm:
+        self.final_gamma = self.lm_head = None
+        if final_norm:  # the output rank: final norm, LM head (bf16, unquantised) and sampling
             self.final_gamma = _seeded_normal((s.hidden,), base_seed + FINAL_NORM_SEED_OFFSET, 0.05, self.device,
                                               on_device_init).to(torch.bfloat16)
+            self.lm_head = _seeded_normal((s.vocab, s.hidden), base_seed + LM_HEAD_SEED_OFFSET, 0.02, self.device,
+                                          on_device_init).to(torch.bfloat16)
         self.softmax_scale = 1.0 / math.sqrt(s.head_dim)
 
     def chunk_context(self, request, history, rows):
@@ -267,6 +271,16 @@ class StageModel:
     def final_norm(self, hidden, residual, out=None):
         s = self.shape
         return K.rms_norm(hidden, residual, self.final_gamma, eps=s.eps, out=out)
+
+    def sample(self, last_hidden, tokens=None):
+        """Greedy output token of each request from its final-normed last hidden
+        row (temperature 0, as the reference samples its one output token)."""
+        rows = last_hidden.shape[0]
+        if tokens is None:
+            tokens = torch.empty(rows, dtype=torch.int32, device=self.device)
+        for r0 in range(0, rows, 8):  # the kernel takes up to 8 rows per weight pass
+            K.lm_head_argmax(last_hidden[r0:r0 + 8], self.lm_head, tokens=tokens[r0:r0 + 8])
+        return tokens
 
     def check_status(self):
         st = int(self.ws.status.item())

@@ -74,6 +74,7 @@ class FoldedRank:
         self.fold = (torch.empty((chunk, h), dtype=torch.bfloat16, device=self.device),
                      torch.empty((chunk, h), dtype=torch.bfloat16, device=self.device))
         self.last_hidden = torch.empty((len(self.request_tokens), h), dtype=torch.bfloat16, device=self.device)
+        self.last_tokens = torch.full((len(self.request_tokens),), -1, dtype=torch.int32, device=self.device)
         self.outputs = {}
         self.contexts = None
         self.stage_events = []
@@ -86,7 +87,9 @@ class FoldedRank:
     def run_bank(self, embeds, *, host_embeds=None, record_events=False):
         """Run this rank's ops for one bank.  ``embeds``: device bf16 [tokens, H]
         per request (list), or None with ``host_embeds`` (pinned host tensors,
-        copied chunk by chunk inside the run)."""
+        copied chunk by chunk inside the run).  On the output rank, returns the
+        final-normed last hidden row of each request and leaves each request's
+        greedy output token in ``last_tokens``."""
         G = self.ranks
         last_stage = self.stage_count - 1
         folded = self.profile == "vpp"
@@ -129,12 +132,15 @@ class FoldedRank:
             if stage == last_stage:
                 if self.keep_all_outputs:
                     self.outputs[batch] = self.model.final_norm(h, r)
-                elif ch.start + ch.rows == self.request_tokens[ch.request]:
+                if ch.start + ch.rows == self.request_tokens[ch.request]:
                     self.model.final_norm(h[-1:], r[-1:], out=self.last_hidden[ch.request:ch.request + 1])
             if record_events:
                 ev1 = torch.cuda.Event(enable_timing=True)
                 ev1.record(stream)
                 self.stage_events.append((batch, stage, ev0, ev1))
+        if self.rank == self.output_rank:
+            # P+1: the one output token of every request (greedy), part of the bank.
+            self.model.sample(self.last_hidden, tokens=self.last_tokens)
         return self.last_hidden
 
     def compute_ms(self):

@@ -267,6 +267,26 @@ def test_swiglu_nvfp4_kernel_bit_exact(K, rows, inter):
     assert np.array_equal(F.unswizzle_scales(act_sf.cpu().numpy(), rows, inter), F.unswizzle_scales(sfo, rows, inter))
 
 
+@pytest.mark.parametrize("rows,dim,vocab", [(1, 1024, 4100), (4, 520, 3000), (8, 5120, 1024)])
+def test_lm_head_argmax_bit_exact(K, rows, dim, vocab):
+    """Logits and greedy tokens of qi_lm_head_argmax equal the oracle's bit for
+    bit; a tie at the maximum goes to the lower index; two calls in a row agree
+    (the workspace resets itself)."""
+    g = torch.Generator().manual_seed(7 + rows)
+    h = torch.randn(rows, dim, generator=g).to(torch.bfloat16)
+    w = (torch.randn(vocab, dim, generator=g) * 0.05).to(torch.bfloat16)
+    _, t0 = P.lm_head_argmax(h.float().numpy(), w.float().numpy())
+    w[vocab - 1] = w[int(t0[0])]  # plant a tie with row 0's winner at the last index
+    ref_logits, ref_tokens = P.lm_head_argmax(h.float().numpy(), w.float().numpy())
+    assert ref_tokens[0] == t0[0]
+    logits = torch.empty(rows, vocab, dtype=torch.float32, device=DEV)
+    tok = K.lm_head_argmax(h.to(DEV), w.to(DEV), logits=logits)
+    again = K.lm_head_argmax(h.to(DEV), w.to(DEV))
+    torch.cuda.synchronize()
+    assert np.array_equal(logits.cpu().numpy(), ref_logits)
+    assert tok.cpu().tolist() == ref_tokens.tolist() == again.cpu().tolist()
+
+
 def _kv_fixture(K, tokens, kvh, d, seed, page_size=16):
     rng = np.random.default_rng(seed)
     pages = (tokens + page_size - 1) // page_size + 5

@@ -101,3 +101,27 @@ def test_tiny_two_stage_forward_free_running():
     want = oracle.forward_chunks(embeds.float().numpy(), chunk)
     rel_l2 = float(np.sqrt(((got - want) ** 2).sum() / (want ** 2).sum()))
     assert rel_l2 < 1e-1, rel_l2
+
+
+def test_bank_output_tokens_are_the_greedy_samples_of_its_final_hidden():
+    """P+1: every request of a bank ends with one greedy output token, sampled
+    on the output rank from the final-normed hidden state of its last prompt
+    token through the bf16 LM head; the oracle's LM head on the same hidden
+    rows and weights picks the same tokens from bit-identical logits."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from qwen_infra_b200.vpp import model as M
+    from qwen_infra_b200.vpp.runner import FoldedRank
+
+    dev = torch.device("cuda:0")
+    tokens = [700, 512, 300]
+    runner = FoldedRank(M.TINY, 0, 1, dev, tokens, 256)
+    g = torch.Generator().manual_seed(5)
+    embeds = [torch.randn(t, M.TINY.hidden, generator=g).to(torch.bfloat16).to(dev) for t in tokens]
+    last = runner.run_bank(embeds)
+    torch.cuda.synchronize()
+    runner.model.check_status()
+    got = runner.last_tokens.cpu().tolist()
+    _, want = P.lm_head_argmax(last.float().cpu().numpy(), runner.model.lm_head.float().cpu().numpy())
+    assert got == want.tolist()
+    assert all(0 <= t < M.TINY.vocab for t in got)

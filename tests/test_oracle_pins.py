@@ -93,3 +93,18 @@ def test_gate_fp8_per_token_scale_properties():
     v = F.bf16_round(out * F.bf16_round(P.sigmoid_f(gate)))
     assert np.all(np.abs(F.e4m3_decode(codes)).max(axis=1) <= 448)
     assert np.all(np.abs(deq - v) <= np.abs(v) * 2 ** -4 + scale[:, None] * 2 ** -9 + 1e-12)
+
+
+def test_lm_head_argmax_oracle_ties_and_nan():
+    from oracle import producers as P
+
+    h = np.ones((2, 8), dtype=np.float32)
+    w = np.zeros((5, 8), dtype=np.float32)
+    w[1] = w[3] = 1.0  # equal best logits at 1 and 3 -> 1
+    w[4] = np.nan
+    logits, tok = P.lm_head_argmax(h, w)
+    assert tok.tolist() == [1, 1]
+    assert logits[0, 1] == 8.0 and np.isnan(logits[0, 4])
+    w2 = np.full((3, 8), -1.0, dtype=np.float32)
+    w2[2] = -0.5  # all negative: the largest (least negative) wins
+    assert P.lm_head_argmax(h, w2)[1].tolist() == [2, 2]
