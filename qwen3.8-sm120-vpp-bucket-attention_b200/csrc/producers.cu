@@ -343,10 +343,16 @@ __global__ void fp8_rows_kernel(const float* __restrict__ w, int k, uint8_t* __r
   for (int c = threadIdx.x; c < k; c += blockDim.x) q[row * k + c] = (uint8_t)f_to_e4m3(__fdiv_rn(w[row * k + c], scale));
 }
 
-// Paged NVFP4 KV -> f16 K [Hkv][tokens][D] and V^T [Hkv][D][v_stride].  The
-// stored values are e2m1 * e4m3 products (exact in f16: at most 5 significant
-// bits, magnitudes 2^-10 .. 2688); the fp32 global multiplier is applied by
-// the attention kernel.  One CTA per (64-token tile, head).
+// Paged NVFP4 K/V of one KV head -> contiguous f16 K [tokens, D] and V^T
+// [D, vt_row].  CTA = 64 tokens of one head; thread = (token, 32-value
+// quarter of D=128 / half of D=64): one 16-byte code load and one 2-byte scale
+// load per K and V, K stored with 16-byte stores (each token's row is written
+// by its threads as one contiguous run), V staged transposed in shared memory
+// and stored as 128-byte V^T row segments in 16-byte pieces.  Values:
+// e2m1 x e4m3, exact in f16 (at most 6 significant bits, magnitudes 2^-10 ..
+// 2688), so the product is taken in f16: a code byte maps to its two e2m1
+// values as f16 through a 256-entry table in shared memory, times the scale
+// converted to f16.  The fp32 global multipliers are applied by the attention.
 template <int D>
 __global__ void __launch_bounds__(256) kv_dequant_kernel(const uint8_t* __restrict__ kc, const uint8_t* __restrict__ vc,
                                                          const uint8_t* __restrict__ ksf, const uint8_t* __restrict__ vsf,
@@ -355,56 +361,69 @@ __global__ void __launch_bounds__(256) kv_dequant_kernel(const uint8_t* __restri
                                                          int64_t sf_page, int64_t sf_row, int64_t sf_head,
                                                          __half* __restrict__ k_out, __half* __restrict__ vt_out,
                                                          int64_t k_head_stride, int64_t vt_head_stride, int64_t vt_row) {
-  __shared__ __half vtile[64][D + 8];
-  const int head = blockIdx.y;
-  const int t0 = blockIdx.x * 64;
-  const float lut[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
-  // Each thread dequantises 8 consecutive values (4 code bytes) of one token.
-  constexpr int PER_TOKEN = D / 8;
-  for (int i = threadIdx.x; i < 64 * PER_TOKEN; i += blockDim.x) {
-    const int tl = i / PER_TOKEN, chunk = i % PER_TOKEN;
-    const int tok = t0 + tl;
-    float kv8[2][8];
-    if (tok < tokens) {
-      const int64_t page = block_table[tok / page_size], entry = tok % page_size;
-      const int64_t dbase = page * data_page + entry * data_row + (int64_t)head * data_head + chunk * 4;
-      const int64_t sbase = page * sf_page + entry * sf_row + (int64_t)head * sf_head + (chunk * 8) / 16;
-#pragma unroll
-      for (int which = 0; which < 2; ++which) {
-        const uint32_t bytes = *reinterpret_cast<const uint32_t*>((which ? vc : kc) + dbase);
-        const float s = e4m3_to_f((which ? vsf : ksf)[sbase]);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t c = (bytes >> (4 * j)) & 0xF;
-          const float m = lut[c & 7];
-          kv8[which][j] = __fmul_rn((c & 8) ? -m : m, s);
-        }
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) kv8[0][j] = kv8[1][j] = 0.0f;
-    }
-    if (tok < tokens) {
-      uint4 packed;
-      __half2* pk = reinterpret_cast<__half2*>(&packed);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) pk[j] = __floats2half2_rn(kv8[0][2 * j], kv8[0][2 * j + 1]);
-      *reinterpret_cast<uint4*>(k_out + head * k_head_stride + (int64_t)tok * D + chunk * 8) = packed;
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) vtile[tl][chunk * 8 + j] = __float2half_rn(kv8[1][j]);
+  constexpr int PARTS = D / 32;          // threads per token
+  constexpr int TOK = 256 / PARTS;       // tokens per pass of the CTA
+  constexpr int VT_PITCH = 64 + 8;       // halves per V^T row in shared memory (16-byte aligned rows)
+  __shared__ __align__(16) __half vtile[D][VT_PITCH];
+  __shared__ __half2 pair_lut[256];  // code byte -> (low-nibble value, high-nibble value)
+  {
+    constexpr float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+    const uint32_t b = threadIdx.x, lo = b & 0xF, hi = b >> 4;
+    const float vlo = (lo & 8) ? -mag[lo & 7] : mag[lo & 7], vhi = (hi & 8) ? -mag[hi & 7] : mag[hi & 7];
+    pair_lut[b] = __floats2half2_rn(vlo, vhi);
   }
   __syncthreads();
-  // Write V^T rows: for each d, 64 consecutive tokens (128 bytes).
-  const int valid = min(64, (int)((vt_row - t0)));
-  for (int i = threadIdx.x; i < D * 32; i += blockDim.x) {
-    const int d = i / 32, pair = i % 32;
-    if (2 * pair < valid) {
-      __half2 v2;
-      v2.x = vtile[2 * pair][d];
-      v2.y = vtile[2 * pair + 1][d];
-      *reinterpret_cast<__half2*>(vt_out + head * vt_head_stride + (int64_t)d * vt_row + t0 + 2 * pair) = v2;
+  const int head = blockIdx.y;
+  const int t0 = blockIdx.x * 64;
+  const int part = threadIdx.x % PARTS;
+  for (int tl = threadIdx.x / PARTS; tl < 64; tl += TOK) {
+    const int tok = t0 + tl;
+    uint4 kcode = make_uint4(0, 0, 0, 0), vcode = kcode;
+    uint32_t kscale = 0, vscale = 0;
+    if (tok < tokens) {
+      const int64_t page = block_table[tok / page_size], entry = tok % page_size;
+      const int64_t dbase = page * data_page + entry * data_row + (int64_t)head * data_head + part * 16;
+      const int64_t sbase = page * sf_page + entry * sf_row + (int64_t)head * sf_head + part * 2;
+      kcode = __ldg(reinterpret_cast<const uint4*>(kc + dbase));
+      vcode = __ldg(reinterpret_cast<const uint4*>(vc + dbase));
+      kscale = __ldg(reinterpret_cast<const unsigned short*>(ksf + sbase));
+      vscale = __ldg(reinterpret_cast<const unsigned short*>(vsf + sbase));
     }
+    const uint32_t kw[4] = {kcode.x, kcode.y, kcode.z, kcode.w}, vw[4] = {vcode.x, vcode.y, vcode.z, vcode.w};
+    uint4 kout[4];
+    __half2* ko = reinterpret_cast<__half2*>(kout);
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {  // two 16-value scale groups
+      const __half ksh = __float2half_rn(e4m3_to_f((kscale >> (8 * g)) & 0xFF));
+      const __half vsh = __float2half_rn(e4m3_to_f((vscale >> (8 * g)) & 0xFF));
+      const __half2 ks2 = __halves2half2(ksh, ksh), vs2 = __halves2half2(vsh, vsh);
+#pragma unroll
+      for (int w = 0; w < 2; ++w) {
+        const uint32_t kb = kw[2 * g + w], vb = vw[2 * g + w];
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) {
+          ko[(2 * g + w) * 4 + j / 2] = __hmul2(pair_lut[(kb >> (4 * j)) & 0xFF], ks2);
+          const __half2 v2 = __hmul2(pair_lut[(vb >> (4 * j)) & 0xFF], vs2);
+          const int d = part * 32 + (2 * g + w) * 8 + j;
+          vtile[d][tl] = __low2half(v2);
+          vtile[d + 1][tl] = __high2half(v2);
+        }
+      }
+    }
+    if (tok < tokens) {
+      uint4* dst = reinterpret_cast<uint4*>(k_out + head * k_head_stride + (int64_t)tok * D + part * 32);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) dst[i] = kout[i];
+    }
+  }
+  __syncthreads();
+  // V^T: row d gets this CTA's 64 tokens (128 bytes) as 8 pieces of 16 bytes.
+  const int valid = min(64, (int)(vt_row - t0));  // vt_row is a multiple of 64, so 64
+  for (int i = threadIdx.x; i < D * 8; i += blockDim.x) {
+    const int d = i / 8, piece = i % 8;
+    if (piece * 8 < valid)
+      *reinterpret_cast<uint4*>(vt_out + head * vt_head_stride + (int64_t)d * vt_row + t0 + piece * 8) =
+          *reinterpret_cast<const uint4*>(&vtile[d][piece * 8]);
   }
 }
 
@@ -631,6 +650,12 @@ int qi_kv_dequant(const QiKvView* kv, const int32_t* block_table, int tokens, vo
   if (!kv || !block_table || tokens < 1 || !k_out || !vt_out || vt_row < tokens || vt_row % 64)
     return (int)cudaErrorInvalidValue;
   if (!kv->k_cache || !kv->v_cache || !kv->k_scales || !kv->v_scales || kv->kvheads < 1 || kv->page_size < 1)
+    return (int)cudaErrorInvalidValue;
+  // 16-byte code loads and 2-byte scale loads per 32 values of a token
+  if (!aligned16(kv->k_cache) || !aligned16(kv->v_cache) || kv->data_page % 16 || kv->data_row % 16 ||
+      kv->data_head % 16 || (reinterpret_cast<uintptr_t>(kv->k_scales) & 1) ||
+      (reinterpret_cast<uintptr_t>(kv->v_scales) & 1) || kv->sf_page % 2 || kv->sf_row % 2 || kv->sf_head % 2 ||
+      !aligned16(k_out) || !aligned16(vt_out))
     return (int)cudaErrorInvalidValue;
   const dim3 grid((tokens + 63) / 64, kv->kvheads);
   const int64_t ks = (int64_t)tokens * kv->head_dim, vs = (int64_t)kv->head_dim * vt_row;
