@@ -35,6 +35,15 @@ import __graft_entry__  # noqa: E402
 METRIC = "4-request prefill bank latency & tok/s at 1/2/4/8 B200; % of NVFP4 TC peak"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
+# DRAM bytes (read + write) of one attention launch from the committed ncu
+# capture (profiles/attention_27b_chunk2048_history30720.md: 2048 query rows
+# over 32768 keys, 549.2 MB read + 33.5 MB written).  The traffic is dominated
+# by K/V reads, which grow with the keys of the launch, so a launch of the
+# bank is credited ATTN_TRAFFIC_BYTES * keys / ATTN_TRAFFIC_KEYS.
+ATTN_TRAFFIC_BYTES = 582.752512e6
+ATTN_TRAFFIC_KEYS = 32768
+ATTN_TRAFFIC_ROWS = 2048
+
 
 def parse():
     p = argparse.ArgumentParser()
@@ -356,8 +365,15 @@ def run_ours(args):
         else:
             peak, pk = peaks["bf16_tflops"], f"bf16_tflops ({peak_kind})"
             bound = "tensor"
+        traffic = traffic_source = None
+        if dom_name == "attention" and args.model == "qwen27b" and args.chunk_size == ATTN_TRAFFIC_ROWS:
+            keys = [start + min(args.chunk_size, args.prompt_tokens - start)
+                    for _ in range(args.requests) for start in range(0, args.prompt_tokens, args.chunk_size)]
+            traffic = ATTN_TRAFFIC_BYTES * (sum(keys) / len(keys)) / ATTN_TRAFFIC_KEYS
+            traffic_source = ("ncu capture (profiles/attention_27b_chunk2048_history30720.md), scaled by the keys "
+                              "of each launch; bytes per launch, averaged over the bank")
         roofline = dict(kernel=dom_name, bound=bound, achieved=dom["achieved"], peak=peak, unit=dom["unit"],
-                        frac=dom["achieved"] / peak, peak_source=pk, traffic=None)
+                        frac=dom["achieved"] / peak, peak_source=pk, traffic=traffic, traffic_source=traffic_source)
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         cpu = cpu_sample(args, os.cpu_count() or 1)
