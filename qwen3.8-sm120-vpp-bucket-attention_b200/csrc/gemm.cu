@@ -57,12 +57,40 @@ struct Params {
   int* status;
 };
 
-// Fused epilogue for one thread's row: v holds its 128 accumulator columns
-// (half h of the 256-column tile starting at n0; for SwiGLU the 64 gate and
-// 64 up columns of output channels (n0/2 + 64h ..)).
+// In-warp transpose of a 32 x 32 matrix of 32-bit words: lane l holds row l
+// in x[0..31] on entry and column l (word l of rows 0..31) on exit; five
+// butterfly stages of shfl_xor, each exchanging half the words with the lane
+// whose bit s differs.
+__device__ __forceinline__ void warp_transpose32(uint32_t* x, int lane) {
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) {
+    const bool upper = (lane & s) != 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if ((j & s) == 0) {  // compile-time pair (j, j|s); selects keep both in registers
+        const uint32_t lo = x[j], hi = x[j | s];
+        const uint32_t recv = __shfl_xor_sync(0xffffffffu, upper ? lo : hi, s);
+        x[j] = upper ? recv : lo;
+        x[j | s] = upper ? hi : recv;
+      }
+    }
+  }
+}
+
+// Fused epilogue of one warp's 32 tile rows (row0 .. row0+31, this thread's
+// row is row0 + lane): v holds the thread's 128 accumulator columns (half h of
+// the 256-column tile starting at n0; for SwiGLU the 64 gate and 64 up
+// columns of output channels (n0/2 + 64h ..)).  bf16 outputs leave the warp
+// transposed, so that every store instruction writes 128 contiguous bytes of
+// one row (a row per thread would make each 16-byte store touch 32 rows:
+// measured, those stores cost the NVFP4 GEMM ~20% through the shared L1 /
+// shared-memory data path).  Rows at or past p.m are not stored.
 template <int kEpi>
-__device__ __forceinline__ void epilogue_rows(const Params& p, float* v, int row, int n0, int half, float alpha) {
+__device__ __forceinline__ void epilogue_rows(const Params& p, float* v, int row0, int lane, int n0, int half,
+                                              float alpha) {
+  const int row = row0 + lane;
   if constexpr (kEpi == QI_EPI_SWIGLU_NVFP4) {
+    if (row >= p.m) return;
     const float g = *p.act_global;
     const int64_t gp = p.act_gp;
     const int ch0 = (n0 >> 1) + half * 64;  // first output channel of this thread's half
@@ -81,34 +109,87 @@ __device__ __forceinline__ void epilogue_rows(const Params& p, float* v, int row
       p.act_sf[sf_offset(row, ch >> 4, gp)] = (uint8_t)code;
     }
   } else if constexpr (kEpi == QI_EPI_F32) {
+    if (row >= p.m) return;
     float* o = static_cast<float*>(p.out) + (int64_t)row * p.ldo + n0 + half * 128;
 #pragma unroll
     for (int j = 0; j < 128; j += 4)
       *reinterpret_cast<float4*>(o + j) = make_float4(__fmul_rn(v[j], alpha), __fmul_rn(v[j + 1], alpha),
                                                       __fmul_rn(v[j + 2], alpha), __fmul_rn(v[j + 3], alpha));
-  } else {
-    const int col0 = n0 + half * 128;
-    float rs = 1.0f;
-    if constexpr (kEpi == QI_EPI_BF16_ROWCOL) rs = p.row_scale[row];
-    uint4* o = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo + col0);
+  }
+}
+
+// bf16 epilogues: the thread's 128 accumulator columns arrive 32 at a time,
+// each block scaled and packed into bf16 pairs at once (so at most 32 fp32
+// values and 64 words are live), then the accumulator is released and the
+// packed row is stored transposed through the warp.
+template <int kEpi>
+__device__ __forceinline__ void pack_bf16_block(const Params& p, const float* v, uint32_t* w, int row, int col0,
+                                                int c0, float alpha) {
+  float rs = 1.0f;
+  if constexpr (kEpi == QI_EPI_BF16_ROWCOL) rs = row < p.m ? p.row_scale[row] : 0.0f;
 #pragma unroll
-    for (int j = 0; j < 128; j += 8) {
-      uint32_t w[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float a, b;
-        if constexpr (kEpi == QI_EPI_BF16_ROWCOL) {
-          a = __fmul_rn(__fmul_rn(v[j + 2 * i], rs), p.col_scale[col0 + j + 2 * i]);
-          b = __fmul_rn(__fmul_rn(v[j + 2 * i + 1], rs), p.col_scale[col0 + j + 2 * i + 1]);
-        } else {
-          a = __fmul_rn(v[j + 2 * i], alpha);
-          b = __fmul_rn(v[j + 2 * i + 1], alpha);
-        }
-        __nv_bfloat162 h2 = __floats2bfloat162_rn(a, b);
-        w[i] = *reinterpret_cast<uint32_t*>(&h2);
-      }
-      o[j / 8] = make_uint4(w[0], w[1], w[2], w[3]);
+  for (int i = 0; i < 16; ++i) {
+    float x0, x1;
+    if constexpr (kEpi == QI_EPI_BF16_ROWCOL) {
+      x0 = __fmul_rn(__fmul_rn(v[2 * i], rs), p.col_scale[col0 + c0 + 2 * i]);
+      x1 = __fmul_rn(__fmul_rn(v[2 * i + 1], rs), p.col_scale[col0 + c0 + 2 * i + 1]);
+    } else {
+      x0 = __fmul_rn(v[2 * i], alpha);
+      x1 = __fmul_rn(v[2 * i + 1], alpha);
     }
+    __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
+    w[i] = *reinterpret_cast<uint32_t*>(&h2);
+  }
+}
+
+__device__ __forceinline__ void store_bf16_transposed(const Params& p, uint32_t* w, int row0, int lane, int col0) {
+#pragma unroll
+  for (int b = 0; b < 2; ++b) {  // two blocks of 32 words = 64 bf16 columns
+    uint32_t* x = w + 32 * b;
+    warp_transpose32(x, lane);  // lane now holds word `lane` (columns 2 lane, 2 lane + 1) of rows row0 + j
+    uint32_t* base = reinterpret_cast<uint32_t*>(static_cast<__nv_bfloat16*>(p.out) + col0 + 64 * b) + lane;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (row0 + j < p.m) base[(int64_t)(row0 + j) * (p.ldo >> 1)] = x[j];
+  }
+}
+
+// One tile's epilogue for one thread (TMEM row = tile row row0 + lane):
+// read the accumulator, call release() (the accumulator may take the next
+// tile), then the fused math and stores.  ok must be warp-uniform.
+template <int kEpi, class Release>
+__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t acc_row, bool ok, int row0, int lane, int n0,
+                                              int half, float alpha, Release release) {
+  if constexpr (kEpi == QI_EPI_BF16 || kEpi == QI_EPI_BF16_ROWCOL) {
+    const int col0 = n0 + half * 128;
+    uint32_t w[64];
+    if (ok) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(acc_row + half * 128 + c * 32, v);
+        pack_bf16_block<kEpi>(p, v, w + 16 * c, row0 + lane, col0, c * 32, alpha);
+      }
+    }
+    release();
+    if (ok) store_bf16_transposed(p, w, row0, lane, col0);
+  } else {
+    float v[128];
+    if (ok) {
+      if constexpr (kEpi == QI_EPI_SWIGLU_NVFP4) {
+        // gate columns [64h, 64h+64) into v[0..64), up columns [128+64h, ...) into v[64..128)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          tmem_ld32(acc_row + half * 64 + c * 32, v + c * 32);
+          tmem_ld32(acc_row + 128 + half * 64 + c * 32, v + 64 + c * 32);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(acc_row + half * 128 + c * 32, v + c * 32);
+      }
+    }
+    release();
+    if (ok) epilogue_rows<kEpi>(p, v, row0, lane, n0, half, alpha);
   }
 }
 
@@ -198,29 +279,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++tcount) {
       const int m0 = (tile % p.m_tiles) * BM, n0 = (tile / p.m_tiles) * BN;
       const int row = m0 + quarter * 32 + lane;
-      const bool in_range = row < p.m;
-      const bool ok = mbar_wait(acc_full, tcount & 1, abort_flag, p.status);
+      // warp-uniform: the epilogue's transposed stores are warp-collective
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full, tcount & 1, abort_flag, p.status));
       tc_fence_after();
-      float v[128];
-      if (ok) {
-        __syncwarp();
-        if constexpr (kEpi == QI_EPI_SWIGLU_NVFP4) {
-          // gate columns [64h, 64h+64) into v[0..64), up columns [128+64h, ...) into v[64..128)
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            tmem_ld32(tmem + lane_off + ACC_COL + half * 64 + c * 32, v + c * 32);
-            tmem_ld32(tmem + lane_off + ACC_COL + 128 + half * 64 + c * 32, v + 64 + c * 32);
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_off + ACC_COL + half * 128 + c * 32, v + c * 32);
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(acc_empty);  // the accumulator may now take the next tile
+      __syncwarp();
+      epilogue_tile<kEpi>(p, tmem + lane_off + ACC_COL, ok, row - lane, lane, n0, half, alpha, [&] {
+        tc_fence_before();
+        mbar_arrive(acc_empty);  // the accumulator may now take the next tile
+      });
       if (!ok) break;
-      if (!in_range) continue;
-      epilogue_rows<kEpi>(p, v, row, n0, half, alpha);
     }
   }
   tc_fence_before();
@@ -396,29 +463,16 @@ __global__ void __launch_bounds__(S_THREADS, 1)
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++tcount) {
       const int m0 = (tile % p.m_tiles) * BM, n0 = (tile / p.m_tiles) * BN;
       const int row = m0 + quarter * 32 + lane;
-      const bool in_range = row < p.m;
       bool ok = mbar_wait(acc_full, tcount & 1, abort_flag, p.status);
       ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
-      float v[128];
-      if (ok) {
-        if constexpr (kEpi == QI_EPI_SWIGLU_NVFP4) {
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            tmem_ld32(tmem + lane_off + ACC_COL + half * 64 + c * 32, v + c * 32);
-            tmem_ld32(tmem + lane_off + ACC_COL + 128 + half * 64 + c * 32, v + 64 + c * 32);
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_off + ACC_COL + half * 128 + c * 32, v + c * 32);
-        }
-      }
-      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty);  // the accumulator may now take the next tile
+      epilogue_tile<kEpi>(p, tmem + lane_off + ACC_COL, ok, row - lane, lane, n0, half, alpha, [&] {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty);  // the accumulator may now take the next tile
+      });
       if (!ok) break;
-      if (!in_range) continue;
-      epilogue_rows<kEpi>(p, v, row, n0, half, alpha);
     }
   }
   tc_fence_before();
@@ -618,29 +672,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     for (int tile = pair; tile < tiles; tile += pairs, ++tcount) {
       const int m0 = (tile % m_tiles2) * 256 + (int)rank * 128, n0 = (tile / m_tiles2) * BN;
       const int row = m0 + quarter * 32 + lane;
-      const bool in_range = row < p.m;
-      const bool ok = mbar_wait_cluster(acc_full, tcount & 1, abort_flag, p.status);
+      // warp-uniform: the epilogue's transposed stores are warp-collective
+      const bool ok = __all_sync(0xffffffffu, mbar_wait_cluster(acc_full, tcount & 1, abort_flag, p.status));
       tc_fence_after();
-      float v[128];
-      if (ok) {
-        __syncwarp();
-        if constexpr (kEpi == QI_EPI_SWIGLU_NVFP4) {
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            tmem_ld32(tmem + lane_off + ACC_COL + half * 64 + c * 32, v + c * 32);
-            tmem_ld32(tmem + lane_off + ACC_COL + 128 + half * 64 + c * 32, v + 64 + c * 32);
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_off + ACC_COL + half * 128 + c * 32, v + c * 32);
-        }
-      }
-      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_remote(leader_acc_empty);  // the accumulator may take the next tile
+      epilogue_tile<kEpi>(p, tmem + lane_off + ACC_COL, ok, row - lane, lane, n0, half, alpha, [&] {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(leader_acc_empty);  // the accumulator may take the next tile
+      });
       if (!ok) break;
-      if (!in_range) continue;
-      epilogue_rows<kEpi>(p, v, row, n0, half, alpha);
     }
   }
   tc_fence_before();
