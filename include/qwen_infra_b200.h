@@ -36,6 +36,7 @@ extern "C" {
 #define QI_STATUS_BAD_KV_SCALE 1
 #define QI_STATUS_WAIT_TIMEOUT 2
 #define QI_STATUS_BAD_SLOT 4
+#define QI_STATUS_BAD_LENGTH 8 /* decode: a length past its page-table row (clamped) */
 
 /* ---- fused residual + RMSNorm -> NVFP4 --------------------------------- */
 
@@ -206,6 +207,48 @@ int qi_paged_prefill_attention_noalloc(const QiKvView* kv, const int32_t* block_
                                        int qheads, const float* k_global, const float* v_global,
                                        float softmax_scale, int* status, cudaStream_t stream);
 
+/* ---- bucket decode attention ------------------------------------------------
+ * One query token per request attends its paged NVFP4 K/V (the cache above),
+ * the KV cut into 256-token tiles and the tiles into tasks.  Replaces the
+ * reference's native-XQA task backend: nvfp4_xqa_assign / nvfp4_xqa_compute /
+ * nvfp4_xqa_resources / nvfp4_xqa_scratch_bytes
+ * (src/qwen_infra/kernels/nvfp4_bucket_xqa.cu:255-288) with its XQATask /
+ * XQARange / XQABucket records (:15-17), plan semantics of
+ * kernels/nvfp4_bucket_xqa.py:19-69, on 16-token pages and head_dim 128. */
+typedef struct QiDecodeTask { int32_t request, begin, end, stride; } QiDecodeTask; /* tiles begin..end step stride */
+typedef struct QiDecodeRange { int32_t first, count; } QiDecodeRange;              /* a request's task slots */
+typedef struct QiDecodeBucket { int32_t begin, end; } QiDecodeBucket;              /* a persistent CTA's slots */
+
+typedef struct QiDecode {
+  const void* q;                 /* bf16 [batch, qheads, 128], 16-byte aligned */
+  QiKvView kv;                   /* head_dim 128; code strides % 16, scale strides % 8 */
+  const int32_t* block_table;    /* [batch, table_width] page ids */
+  const int32_t* lengths;        /* [batch] keys per request, 0 .. table_width * page_size */
+  QiDecodeTask* tasks;           /* [ctas + batch - 1]  plan, written by qi_decode_assign */
+  QiDecodeRange* requests;       /* [batch] */
+  QiDecodeBucket* buckets;       /* [ctas] */
+  int32_t* header;               /* [4]: budget (splits when cyclic), tasks, active CTAs, max tasks per request */
+  int32_t* semaphores;           /* [batch * Hkv] zero before the first call; calls leave them zero */
+  void* scratch;                 /* qi_decode_scratch_bytes(ctas + batch - 1, Hkv) bytes, 16-byte aligned */
+  void* out;                     /* bf16 [batch, qheads, 128]; e4m3 bytes of the same shape with gate */
+  const void* gate;              /* NULL, or bf16 [batch, qheads * 128]: gated FP8 output */
+  const float* out_scale;        /* with gate: static fp32 output scale */
+  const float *k_global, *v_global; /* cache dequantisation multipliers */
+  int* status;
+  int batch, ctas, table_width;  /* 1..32 requests, batch <= ctas <= 340 task slots */
+  int mode;                      /* 0 intervals, 1 cyclic, 2 aligned */
+  int persistent;                /* mode 0 only: ctas CTAs each run their bucket of slots */
+  int qheads;                    /* qheads / Hkv <= 16 */
+  float softmax_scale;
+} QiDecode;
+
+int qi_decode_assign(const QiDecode* p, cudaStream_t stream);
+int qi_decode_attention(const QiDecode* p, cudaStream_t stream);
+/* values[8]: sizeof(QiDecode), registers, shared bytes, local bytes, resident
+ * CTAs per SM, sizeof(QiDecodeTask), sizeof(QiDecodeRange), sizeof(QiDecodeBucket). */
+int qi_decode_resources(int* values);
+uint64_t qi_decode_scratch_bytes(int capacity, int kvheads);
+
 /* ---- weight preparation ------------------------------------------------- */
 int qi_nvfp4_quantize(const float* w, int64_t rows, int k, const float* global_scale, void* q, void* scales,
                       cudaStream_t stream);
@@ -215,7 +258,7 @@ int qi_fp8_quantize_rows(const float* w, int rows, int k, void* q, float* scales
  * n/2 bytes packed eight at a time; e4m3[n]; ex[2n] = (fexp, sigmoid) pairs. */
 int qi_convert_probe(const float* in, void* e2m1_pairs, void* e4m3, float* ex, int n, cudaStream_t stream);
 
-/* Host-only: sizeof(RefFront, QiFront, QiGemm, QiKvView, QiAttention) for ABI checks. */
+/* Host-only: sizeof(RefFront, QiFront, QiGemm, QiKvView, QiAttention, QiDecode) for ABI checks. */
 int qi_abi_struct_sizes(int* out);
 
 #ifdef __cplusplus

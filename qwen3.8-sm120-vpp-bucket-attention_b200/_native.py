@@ -71,6 +71,16 @@ class QiAttention(ct.Structure):
     )
 
 
+class QiDecode(ct.Structure):
+    _fields_ = (
+        [("q", _vp), ("kv", QiKvView)]
+        + [(n, _vp) for n in ("block_table", "lengths", "tasks", "requests", "buckets", "header", "semaphores",
+                              "scratch", "out", "gate", "out_scale", "k_global", "v_global", "status")]
+        + [(n, _i32) for n in ("batch", "ctas", "table_width", "mode", "persistent", "qheads")]
+        + [("softmax_scale", _f32)]
+    )
+
+
 EXPORTS = {
     "nvfp4_norm_pack_launch": ([_vp] * 7 + [_i32, _vp], _i32),
     "nvfp4_norm_pack_metadata": ([ct.POINTER(_i32)], _i32),
@@ -93,6 +103,10 @@ EXPORTS = {
     "qi_fp8_quantize_rows": ([_vp, _i32, _i32, _vp, _vp, _vp], _i32),
     "qi_abi_struct_sizes": ([ct.POINTER(_i32)], _i32),
     "qi_convert_probe": ([_vp, _vp, _vp, _vp, _i32, _vp], _i32),
+    "qi_decode_assign": ([ct.POINTER(QiDecode), _vp], _i32),
+    "qi_decode_attention": ([ct.POINTER(QiDecode), _vp], _i32),
+    "qi_decode_resources": ([ct.POINTER(_i32)], _i32),
+    "qi_decode_scratch_bytes": ([_i32, _i32], ct.c_uint64),
 }
 
 _lib = None
@@ -109,10 +123,10 @@ def lib():
             fn = getattr(handle, name)
             fn.argtypes = args
             fn.restype = res
-        sizes = (ct.c_int * 5)()
+        sizes = (ct.c_int * 6)()
         if handle.qi_abi_struct_sizes(sizes):
             raise RuntimeError("qi_abi_struct_sizes failed")
-        expected = [ct.sizeof(c) for c in (RefFront, QiFront, QiGemm, QiKvView, QiAttention)]
+        expected = [ct.sizeof(c) for c in (RefFront, QiFront, QiGemm, QiKvView, QiAttention, QiDecode)]
         if list(sizes) != expected:
             raise RuntimeError(f"C ABI struct sizes {list(sizes)} != ctypes {expected}")
         _lib = handle

@@ -689,6 +689,7 @@ int qi_abi_struct_sizes(int* out) {
   out[2] = (int)sizeof(QiGemm);
   out[3] = (int)sizeof(QiKvView);
   out[4] = (int)sizeof(QiAttention);
+  out[5] = (int)sizeof(QiDecode);
   return 0;
 }
 
