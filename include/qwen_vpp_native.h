@@ -13,6 +13,10 @@
  *                  here credits (grant) and publication for a peer-to-peer copy
  *   qv_copy_message <- DmaEdge D2H/H2D segment copies (native/dma_edge.cpp:135-194),
  *                  here one device-to-device copy per plane segment over NVLink
+ *   qv_kvcopy_*  <- KvCopy (native/kv_copy.h:10-45, kv_copy.cpp:62-401): KV page
+ *                  offload / reload between device byte buffers and a pinned host
+ *                  pool, one cudaMemcpyAsync (or cudaMemcpy2DAsync for a strided
+ *                  run of whole fragments) per piece instead of batched copies
  */
 #ifndef QWEN_VPP_NATIVE_H
 #define QWEN_VPP_NATIVE_H
@@ -105,6 +109,45 @@ int qv_copy_message(int device, void* stream, void* residual_ready, void* hidden
                     const void* src_residual, void* dst_hidden, void* dst_residual, uint64_t plane_bytes,
                     uint64_t segment_bytes, void* ipc_done, void* local_done);
 int qv_stream_wait_event(int device, void* stream, void* event);
+
+/* ---- KV page copy engine ---------------------------------------------------
+ * Copy runs are int64 rows [tensor, device offset, host offset, bytes,
+ * fragments, device stride, host stride]; gates (optional) int64 rows [flag
+ * index, epoch > 0]: a store publishes flags[gate] = epoch (release) when all
+ * of its gate's bytes landed on the host, a load starts a gate's runs once
+ * flags[gate] == epoch (acquire).  segment_bytes 4, 8 or 16 MiB; 1..8 jobs;
+ * runs per job (and copy calls per segment) <= max_runs <= 2^20.  The host
+ * pool must be pinned.  Errors: NULL, -1 (invalid arguments, nothing done)
+ * or -4 (engine failure: CUDA error, job deadline, closed; terminal), with
+ * qv_kvcopy_last_error(). */
+typedef struct QvKvCopyResult {
+  uint64_t job_id, generation, bytes, segments;
+  int32_t cancelled;
+  float device_ms;
+  uint64_t first_issue_ns, last_done_ns;
+} QvKvCopyResult;
+
+const char* qv_kvcopy_last_error(void);
+void* qv_kvcopy_create(int device, void* const* buffers, const uint64_t* buffer_bytes, int count, void* host,
+                       uint64_t host_bytes, uint64_t segment_bytes, uint32_t max_jobs, uint32_t max_runs, int pitched);
+void qv_kvcopy_destroy(void* engine);
+/* 1 admitted, 0 every job slot busy (poll, then retry), -1 invalid. ids increase. */
+int qv_kvcopy_submit(void* engine, uint64_t id, uint64_t generation, const int64_t* runs, int64_t count, int store,
+                     void* producer_stream, const int64_t* gates);
+int qv_kvcopy_set_ready(void* engine, int64_t* flags, int64_t count);
+int qv_kvcopy_cancel(void* engine, uint64_t id, uint64_t generation); /* 1 found, 0 not */
+/* Finished jobs (harvested) / live jobs (not harvested): returns the count,
+ * writes at most cap results. */
+int qv_kvcopy_poll(void* engine, QvKvCopyResult* out, int cap);
+int qv_kvcopy_snapshot(void* engine, QvKvCopyResult* out, int cap);
+int qv_kvcopy_wait(void* engine, const uint64_t* ids, int count, uint32_t timeout_ms); /* 0, -2 deadline */
+int qv_kvcopy_drain(void* engine, uint32_t timeout_ms);                             /* 0, -2 deadline */
+int qv_kvcopy_close(void* engine);
+/* Host-only validation of a job's runs (no device use): units (gates), pieces
+ * after collapsing contiguous runs, and bytes. */
+int qv_kvcopy_plan(const uint64_t* buffer_bytes, int count, uint64_t host_bytes, const int64_t* runs, int64_t rows,
+                   const int64_t* gates, int64_t flag_count, uint32_t max_runs, int64_t* units_out,
+                   int64_t* pieces_out, uint64_t* bytes_out);
 
 #ifdef __cplusplus
 }

@@ -20,7 +20,7 @@ KERNEL_LIB = PKG / "libqwen_infra_b200.so"
 TRANSPORT_LIB = PKG / "libqwen_vpp_native.so"
 
 KERNEL_SOURCES = ["producers.cu", "gemm.cu", "attention.cu", "attention_noalloc.cu", "lm_head.cu", "decode.cu"]
-TRANSPORT_SOURCES = ["wire.cpp", "slot_pool.cpp", "edges.cpp", "transport_abi.cpp"]
+TRANSPORT_SOURCES = ["wire.cpp", "slot_pool.cpp", "edges.cpp", "transport_abi.cpp", "kv_copy.cpp"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -30,6 +30,12 @@ class QvBoundary(ct.Structure):
         return {name: getattr(self, name) for name, _ in self._fields_}
 
 
+class QvKvCopyResult(ct.Structure):
+    _fields_ = [("job_id", ct.c_uint64), ("generation", ct.c_uint64), ("bytes", ct.c_uint64),
+                ("segments", ct.c_uint64), ("cancelled", ct.c_int32), ("device_ms", ct.c_float),
+                ("first_issue_ns", ct.c_uint64), ("last_done_ns", ct.c_uint64)]
+
+
 class QvTicket(ct.Structure):
     _fields_ = [("ring_id", _u64), ("sequence", _u64), ("generation", _u64), ("slot_id", _u32)]
 
@@ -82,6 +88,19 @@ SIGS = {
     "qv_event_query": ([_vp], _i32),
     "qv_copy_message": ([_i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _u64, _u64, _vp, _vp], _i32),
     "qv_stream_wait_event": ([_i32, _vp, _vp], _i32),
+    "qv_kvcopy_last_error": ([], ct.c_char_p),
+    "qv_kvcopy_create": ([_i32, ct.POINTER(_vp), ct.POINTER(_u64), _i32, _vp, _u64, _u64, _u32, _u32, _i32], _vp),
+    "qv_kvcopy_destroy": ([_vp], None),
+    "qv_kvcopy_submit": ([_vp, _u64, _u64, ct.POINTER(_i64), _i64, _i32, _vp, ct.POINTER(_i64)], _i32),
+    "qv_kvcopy_set_ready": ([_vp, ct.POINTER(_i64), _i64], _i32),
+    "qv_kvcopy_cancel": ([_vp, _u64, _u64], _i32),
+    "qv_kvcopy_poll": ([_vp, ct.POINTER(QvKvCopyResult), _i32], _i32),
+    "qv_kvcopy_snapshot": ([_vp, ct.POINTER(QvKvCopyResult), _i32], _i32),
+    "qv_kvcopy_wait": ([_vp, ct.POINTER(_u64), _i32, _u32], _i32),
+    "qv_kvcopy_drain": ([_vp, _u32], _i32),
+    "qv_kvcopy_close": ([_vp], _i32),
+    "qv_kvcopy_plan": ([ct.POINTER(_u64), _i32, _u64, ct.POINTER(_i64), _i64, ct.POINTER(_i64), _i64, _u32,
+                        ct.POINTER(_i64), ct.POINTER(_i64), ct.POINTER(_u64)], _i32),
 }
 
 _lib = None
