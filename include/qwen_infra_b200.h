@@ -124,6 +124,13 @@ int qi_lm_head_workspace_bytes(void);
 /* ---- attention output x sigmoid(gate) -> FP8 (per-token scale) --------- */
 int qi_gate_fp8(const void* out, const void* gate, int64_t out_row, int64_t gate_row, void* fp8, int64_t fp8_row,
                 float* scale, int rows, int cols, cudaStream_t stream);
+/* The same with the gate read per head: column c at gate + row * gate_row +
+ * (c / head_dim) * gate_head_stride + c % head_dim (elements), e.g. in place in
+ * the QKV projection output (gate = qkv + D, gate_head_stride = 2D), which
+ * spares the front kernel its gate copy. */
+int qi_gate_fp8_heads(const void* out, const void* gate, int64_t out_row, int64_t gate_row, int64_t gate_head_stride,
+                      int head_dim, void* fp8, int64_t fp8_row, float* scale, int rows, int cols,
+                      cudaStream_t stream);
 
 /* ---- tcgen05 GEMM: D[m, n] = A[m, k] . B[n, k]^T ------------------------ */
 #define QI_GEMM_NVFP4 0 /* kind::mxf4nvf4, E2M1 with 16-element E4M3 block scales */

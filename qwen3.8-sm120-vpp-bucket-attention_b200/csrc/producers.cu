@@ -246,9 +246,13 @@ __global__ void __launch_bounds__(256) front_kernel(QiFront p) {
 }
 
 // One CTA per row, thread t owns 16 consecutive columns.
+// The gate of column c sits at gate + row * gate_row + (c / head_dim) *
+// head_stride + c % head_dim: a compact [rows, cols] gate (head_dim = cols),
+// or the gate halves read in place from the QKV projection's per-head
+// [q(D) | gate(D)] blocks (head_dim = D, head_stride = 2D).
 __global__ void gate_fp8_kernel(const __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ gate,
-                                int64_t out_row, int64_t gate_row, uint8_t* __restrict__ fp8, int64_t fp8_row,
-                                float* __restrict__ scale_out, int cols) {
+                                int64_t out_row, int64_t gate_row, int head_dim, int64_t head_stride,
+                                uint8_t* __restrict__ fp8, int64_t fp8_row, float* __restrict__ scale_out, int cols) {
   __shared__ float scratch[33];
   const int64_t row = blockIdx.x;
   const int t = threadIdx.x;
@@ -258,7 +262,7 @@ __global__ void gate_fp8_kernel(const __nv_bfloat16* __restrict__ out, const __n
   if (active) {
     float o[16], g[16];
     load16_bf16(out + row * out_row + 16 * t, o);
-    load16_bf16(gate + row * gate_row + 16 * t, g);
+    load16_bf16(gate + row * gate_row + (int64_t)(16 * t / head_dim) * head_stride + (16 * t) % head_dim, g);
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       v[j] = bf16r(__fmul_rn(o[j], bf16r(sigmoid_f(g[j]))));
@@ -609,18 +613,26 @@ int qi_swiglu_nvfp4(const void* gate_up, int64_t gu_row, int rows, int inter, co
   return (int)cudaPeekAtLastError();
 }
 
-int qi_gate_fp8(const void* out, const void* gate, int64_t out_row, int64_t gate_row, void* fp8, int64_t fp8_row,
-                float* scale, int rows, int cols, cudaStream_t stream) {
+int qi_gate_fp8_heads(const void* out, const void* gate, int64_t out_row, int64_t gate_row, int64_t gate_head_stride,
+                      int head_dim, void* fp8, int64_t fp8_row, float* scale, int rows, int cols,
+                      cudaStream_t stream) {
   QI_BIND(stream, out);
-  if (rows < 1 || cols < 16 || cols % 16 || cols > 16384 || !out || !gate || !fp8 || !scale)
+  if (rows < 1 || cols < 16 || cols % 16 || cols > 16384 || !out || !gate || !fp8 || !scale || head_dim < 16 ||
+      head_dim % 16 || cols % head_dim || gate_head_stride < 0 || gate_head_stride % 8 ||
+      (cols > head_dim && gate_head_stride < head_dim))
     return (int)cudaErrorInvalidValue;
   if (!aligned16(out) || !aligned16(gate) || !aligned16(fp8) || out_row % 8 || gate_row % 8 || fp8_row % 16)
     return (int)cudaErrorInvalidValue;
   const int threads = ((cols / 16) + 31) / 32 * 32;
   gate_fp8_kernel<<<rows, threads, 0, stream>>>(static_cast<const __nv_bfloat16*>(out),
-                                                static_cast<const __nv_bfloat16*>(gate), out_row, gate_row,
-                                                static_cast<uint8_t*>(fp8), fp8_row, scale, cols);
+                                                static_cast<const __nv_bfloat16*>(gate), out_row, gate_row, head_dim,
+                                                gate_head_stride, static_cast<uint8_t*>(fp8), fp8_row, scale, cols);
   return (int)cudaPeekAtLastError();
+}
+
+int qi_gate_fp8(const void* out, const void* gate, int64_t out_row, int64_t gate_row, void* fp8, int64_t fp8_row,
+                float* scale, int rows, int cols, cudaStream_t stream) {
+  return qi_gate_fp8_heads(out, gate, out_row, gate_row, 0, cols, fp8, fp8_row, scale, rows, cols, stream);
 }
 
 int qi_nvfp4_quantize(const float* w, int64_t rows, int k, const float* global_scale, void* q, void* scales,

@@ -175,20 +175,36 @@ def qk_rope_kv_append(qkv, positions, q_weight, k_weight, cos_sin, slots, kv, k_
     p.data_page, p.data_row, p.data_head = kv.k.stride(0), kv.k.stride(1), kv.k.stride(2)
     p.sf_page, p.sf_row, p.sf_head = kv.ks.stride(0), kv.ks.stride(1), kv.ks.stride(2)
     p.eps, p.weight_offset = eps, weight_offset
-    N.check(_run("qk_rope_kv_append", rows * (qkv.shape[1] * 2 + 2 * qheads * d * 2 + kvheads * (d + d // 8) + d * 4), "B", qkv.device, lambda: N.lib().qi_qk_rope_kv_append(ct.byref(p), _stream(qkv.device))), "qi_qk_rope_kv_append")
+    # bytes per row: read q, k, v (and the gate when split) + cos/sin; write q
+    # (and the gate), K/V codes and scales
+    split = 2 * qheads * d * 2 if gate is not None else 0
+    work = rows * ((qheads + 2 * kvheads) * d * 2 + d * 4 + qheads * d * 2 + kvheads * (d + d // 8) + split)
+    N.check(_run("qk_rope_kv_append", work, "B", qkv.device,
+                 lambda: N.lib().qi_qk_rope_kv_append(ct.byref(p), _stream(qkv.device))), "qi_qk_rope_kv_append")
     return q, gate
 
 
-def gate_fp8(out, gate, *, fp8=None, scale=None):
-    """bf16(out * bf16(sigmoid(gate))) -> E4M3 with a per-row fp32 scale."""
+def gate_fp8(out, gate, *, fp8=None, scale=None, head_dim=None, head_stride=None):
+    """bf16(out * bf16(sigmoid(gate))) -> E4M3 with a per-row fp32 scale.
+    ``gate`` is a compact [rows, cols] tensor, or (with ``head_dim`` and
+    ``head_stride``) a view whose head h starts h * head_stride elements into
+    each row, e.g. ``qkv[:, D:]`` with head_stride 2D (the gate halves of the
+    QKV projection, read in place)."""
     _cuda(out, gate)
     rows, cols = out.shape
+    hd = cols if head_dim is None else head_dim
+    hs = 0 if head_stride is None else head_stride
+    if gate.stride(-1) != 1 or gate.shape[0] != rows or (head_dim is None and gate.shape[1] != cols) \
+            or (head_dim is not None and (cols // hd - 1) * hs + hd > gate.shape[1]):
+        raise ValueError("gate must cover [rows, cols] (compact or per head)")
     if fp8 is None:
         fp8 = torch.empty((rows, cols), dtype=torch.uint8, device=out.device)
     if scale is None:
         scale = torch.empty(rows, dtype=torch.float32, device=out.device)
-    N.check(_run("gate_fp8", rows * (cols * 5 + 4), "B", out.device, lambda: N.lib().qi_gate_fp8(_ptr(out), _ptr(gate), out.stride(0), gate.stride(0), _ptr(fp8), fp8.stride(0),
-                                _ptr(scale), rows, cols, _stream(out.device))), "qi_gate_fp8")
+    N.check(_run("gate_fp8", rows * (cols * 5 + 4), "B", out.device,
+                 lambda: N.lib().qi_gate_fp8_heads(_ptr(out), _ptr(gate), out.stride(0), gate.stride(0), hs, hd,
+                                                   _ptr(fp8), fp8.stride(0), _ptr(scale), rows, cols,
+                                                   _stream(out.device))), "qi_gate_fp8_heads")
     return fp8, scale
 
 

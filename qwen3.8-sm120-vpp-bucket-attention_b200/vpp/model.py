@@ -158,7 +158,6 @@ class Workspace:
         self.res1 = torch.empty((max_rows, h), dtype=torch.bfloat16, **e)
         self.qkv = torch.empty((max_rows, s.qkv_out), dtype=torch.bfloat16, **e)
         self.q = torch.empty((max_rows, s.qheads * d), dtype=torch.bfloat16, **e)
-        self.gate = torch.empty((max_rows, s.qheads * d), dtype=torch.bfloat16, **e)
         self.att = torch.empty((max_rows, s.qheads * d), dtype=torch.bfloat16, **e)
         self.a8 = torch.empty((max_rows, s.qheads * d), dtype=torch.uint8, **e)
         self.s8 = torch.empty(max_rows, dtype=torch.float32, **e)
@@ -229,16 +228,18 @@ class StageModel:
         qkv = K.gemm_nvfp4(q_in, sf_in, w.qkv.q, w.qkv.sf, m=rows, n=s.qkv_out, k=h, alpha=w.alpha_qkv,
                            out=ws.qkv[:rows])
         kv = self.kv[layer]
-        q, gate = K.qk_rope_kv_append(qkv, ctx.positions, w.q_norm, w.k_norm, self.rope, ctx.slots, kv, self.kg,
-                                      self.vg, qheads=s.qheads, kvheads=s.kvheads, head_dim=d, eps=s.eps,
-                                      q=ws.q[:rows], gate=ws.gate[:rows], status=ws.status)
+        # The gate halves stay in the QKV output and the gate epilogue reads
+        # them there (no split copy).
+        q, _ = K.qk_rope_kv_append(qkv, ctx.positions, w.q_norm, w.k_norm, self.rope, ctx.slots, kv, self.kg,
+                                   self.vg, qheads=s.qheads, kvheads=s.kvheads, head_dim=d, eps=s.eps,
+                                   q=ws.q[:rows], want_gate=False, status=ws.status)
         tokens = ctx.history + rows
         kd, vt = ws.kv_views(s, tokens)
         K.kv_dequant(kv, ctx.block_table, tokens, k_out=kd, vt_out=vt)
         att = K.prefill_attention(q, kd, vt, history=ctx.history, qheads=s.qheads, kvheads=s.kvheads, head_dim=d,
                                   k_global=self.kg, v_global=self.vg, out=ws.att[:rows],
                                   softmax_scale=self.softmax_scale, status=ws.status)
-        a8, s8 = K.gate_fp8(att, gate, fp8=ws.a8[:rows], scale=ws.s8[:rows])
+        a8, s8 = K.gate_fp8(att, qkv[:, d:], fp8=ws.a8[:rows], scale=ws.s8[:rows], head_dim=d, head_stride=2 * d)
         o = K.gemm_e4m3(a8, w.o_q, m=rows, n=h, k=s.qheads * d, row_scale=s8, col_scale=w.o_scale,
                         out=ws.o[:rows])
         q_m, sf_m, _ = K.norm_pack(o, res1, w.ln_post, self.g_norm, eps=s.eps, q=ws.q_m[:rows], scales=ws.sf_m,

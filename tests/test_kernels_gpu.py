@@ -180,6 +180,22 @@ def test_gate_fp8_bit_exact(K):
     assert np.array_equal(fp8.cpu().numpy(), co)
 
 
+def test_gate_fp8_reads_gate_in_place_from_qkv_rows(K):
+    """The model path's gate operand: per head h the gate half of the QKV
+    projection row ([q(D) | gate(D)] blocks, then K and V heads), read with a
+    head stride of 2D; same bytes as the compact gate."""
+    rows, heads, d, kvh = 260, 16, 128, 2
+    qkv = _bf16((rows, (2 * heads + 2 * kvh) * d), 33, 2.0)
+    out = _bf16((rows, heads * d), 34)
+    gate = qkv[:, : 2 * heads * d].reshape(rows, heads, 2, d)[:, :, 1].reshape(rows, heads * d)
+    qd = qkv.to(DEV)
+    fp8, scale = K.gate_fp8(out.to(DEV), qd[:, d:], head_dim=d, head_stride=2 * d)
+    co, so = P.gate_fp8(out.float().numpy(), gate.float().numpy())
+    torch.cuda.synchronize()
+    assert np.array_equal(scale.cpu().numpy(), so)
+    assert np.array_equal(fp8.cpu().numpy(), co)
+
+
 def test_weight_quantizers_bit_exact(K):
     w = torch.randn(512, 1024, generator=torch.Generator().manual_seed(41)) * 0.02
     qo, sfo, go = P.quantize_weight_nvfp4(w.numpy())
