@@ -58,6 +58,13 @@ QI_DEV void report(int* status, int code) {
 // fp32 helpers: one IEEE rounding per operation, never contracted.
 // ---------------------------------------------------------------------------
 QI_DEV float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+// Two values rounded to bf16 (RN-even) with one packed conversion.
+QI_DEV void bf16r2(float& a, float& b) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));  // first source -> upper half
+  a = __uint_as_float(r << 16);
+  b = __uint_as_float(r & 0xFFFF0000u);
+}
 
 QI_DEV float e4m3_to_f(uint32_t c) {
   const uint32_t e = (c >> 3) & 0xF, m = c & 7;
@@ -69,6 +76,12 @@ QI_DEV uint32_t f_to_e4m3(float x) {
   uint16_t r;
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.0f), "f"(x));
   return r & 0xFFu;
+}
+// Two E4M3 codes in one conversion: lo in bits 0-7, hi in bits 8-15.
+QI_DEV uint32_t f2_to_e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 
 // Eight fp32 values -> eight E2M1 codes packed in 32 bits, element 0 in the
@@ -114,7 +127,11 @@ QI_DEV float fexp(float x) {
   if (t >= 128.0f) return __int_as_float(0x7f800000);
   if (t <= -150.0f) return 0.0f;
   const float tc = fminf(fmaxf(t, -149.0f), 127.0f);
-  const float n = rintf(tc);
+  // n = rint(tc): adding 1.5 * 2^23 leaves a unit last place, so the sum is tc
+  // rounded to the nearest integer (ties to even) and its low bits hold n; two
+  // FMA-pipe adds instead of the quarter-rate FRND / F2I conversions.
+  const float nb = __fadd_rn(tc, 12582912.0f);
+  const float n = __fsub_rn(nb, 12582912.0f);
   const float f = __fsub_rn(tc, n);
   float p = kExpC6;
   p = __fadd_rn(__fmul_rn(p, f), kExpC5);
@@ -123,7 +140,7 @@ QI_DEV float fexp(float x) {
   p = __fadd_rn(__fmul_rn(p, f), kExpC2);
   p = __fadd_rn(__fmul_rn(p, f), kExpC1);
   p = __fadd_rn(__fmul_rn(p, f), kExpC0);
-  const int ni = (int)n;
+  const int ni = __float_as_int(nb) - 0x4B400000;
   const int h1 = ni >> 1, h2 = ni - h1;
   const float s1 = __int_as_float((h1 + 127) << 23), s2 = __int_as_float((h2 + 127) << 23);
   return __fmul_rn(__fmul_rn(p, s1), s2);

@@ -124,128 +124,141 @@ __global__ void norm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bflo
   }
 }
 
-// QK-norm + RoPE + gate split + NVFP4 paged append.  One warp per (row, head):
-// lane l owns E2 = D/64 consecutive elements of each rotary half.
+// QK-norm + RoPE + gate split + NVFP4 paged append.  One CTA per row, warp w
+// takes heads w, w + 8, ...; lane l owns E2 = D/64 consecutive elements of
+// each rotary half.  The row's position, its cos/sin values and the norm
+// weights are loaded once per row and reused by every head.
 template <int E2>
 __global__ void __launch_bounds__(256) front_kernel(QiFront p) {
   constexpr int D = E2 * 64, HALF = D / 2;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = blockIdx.x;
-  const int head = blockIdx.y * 8 + warp;
-  if (head >= p.qheads + p.kvheads) return;
-  const bool is_k = head >= p.qheads;
-  const int local = is_k ? head - p.qheads : head;
-  const __nv_bfloat16* qkv = static_cast<const __nv_bfloat16*>(p.qkv);
-  const int64_t base = row * p.input_row + (is_k ? (int64_t)p.qheads * 2 * D + (int64_t)local * D : (int64_t)local * 2 * D);
   const int d0 = lane * E2;
-  float x[E2], y[E2];
-#pragma unroll
-  for (int i = 0; i < E2; ++i) {
-    x[i] = __bfloat162float(qkv[base + d0 + i]);
-    y[i] = __bfloat162float(qkv[base + HALF + d0 + i]);
-  }
-  float ss = __fmul_rn(x[0], x[0]);
-  ss = __fadd_rn(ss, __fmul_rn(y[0], y[0]));
-#pragma unroll
-  for (int i = 1; i < E2; ++i) {
-    ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));
-    ss = __fadd_rn(ss, __fmul_rn(y[i], y[i]));
-  }
-  ss = warp_sum_butterfly(ss);
-  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), p.eps)));
-  const __nv_bfloat16* w = static_cast<const __nv_bfloat16*>(is_k ? p.k_weight : p.q_weight);
+  const __nv_bfloat16* qkv = static_cast<const __nv_bfloat16*>(p.qkv);
   const int64_t pos = p.pos_long ? static_cast<const int64_t*>(p.positions)[row]
                                  : static_cast<const int32_t*>(p.positions)[row];
-#pragma unroll
-  for (int i = 0; i < E2; ++i) {
-    const float a = bf16r(__fmul_rn(__fmul_rn(x[i], inv), __fadd_rn(__bfloat162float(w[d0 + i]), p.weight_offset)));
-    const float b =
-        bf16r(__fmul_rn(__fmul_rn(y[i], inv), __fadd_rn(__bfloat162float(w[HALF + d0 + i]), p.weight_offset)));
-    float c, s;
-    const int64_t co = pos * p.cos_row + d0 + i;
-    if (p.cos_float) {
-      c = static_cast<const float*>(p.cos_sin)[co];
-      s = static_cast<const float*>(p.cos_sin)[co + HALF];
-    } else {
-      c = __bfloat162float(static_cast<const __nv_bfloat16*>(p.cos_sin)[co]);
-      s = __bfloat162float(static_cast<const __nv_bfloat16*>(p.cos_sin)[co + HALF]);
-    }
-    x[i] = bf16r(__fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s)));
-    y[i] = bf16r(__fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s)));
-  }
-  if (!is_k) {
-    __nv_bfloat16* q = static_cast<__nv_bfloat16*>(p.q) + row * p.q_row + (int64_t)local * D;
+  float cs[E2], sn[E2], wq[2][E2], wk[2][E2];
+  {
+    const __nv_bfloat16* qw = static_cast<const __nv_bfloat16*>(p.q_weight);
+    const __nv_bfloat16* kw = static_cast<const __nv_bfloat16*>(p.k_weight);
 #pragma unroll
     for (int i = 0; i < E2; ++i) {
-      q[d0 + i] = __float2bfloat16_rn(x[i]);
-      q[HALF + d0 + i] = __float2bfloat16_rn(y[i]);
-    }
-    if (p.gate) {
-      __nv_bfloat16* g = static_cast<__nv_bfloat16*>(p.gate) + row * p.gate_row + (int64_t)local * D;
-#pragma unroll
-      for (int i = 0; i < E2; ++i) {
-        g[d0 + i] = qkv[base + D + d0 + i];
-        g[HALF + d0 + i] = qkv[base + D + HALF + d0 + i];
-      }
-    }
-    return;
-  }
-  if (row >= p.slot_rows) return;
-  const int64_t slot = p.slot_long ? static_cast<const int64_t*>(p.slots)[row]
-                                   : static_cast<const int32_t*>(p.slots)[row];
-  if (slot < 0) return;  // padding token: nothing to append
-  if (slot >= (int64_t)p.pages * p.page_size) {
-    if (lane == 0) report(p.status, kStatusBadSlot);
-    return;
-  }
-  const float kg = *p.k_global, vg = *p.v_global;
-  if (!(isfinite(kg) && kg > 0.0f && isfinite(vg) && vg > 0.0f)) {
-    if (lane == 0) report(p.status, kStatusBadKvScale);
-    return;
-  }
-  const int64_t page = slot / p.page_size, entry = slot % p.page_size;
-  const int64_t data = page * p.data_page + entry * p.data_row + (int64_t)local * p.data_head;
-  const int64_t sfo = page * p.sf_page + entry * p.sf_row + (int64_t)local * p.sf_head;
-  const int64_t vbase = row * p.input_row + (int64_t)p.qheads * 2 * D + (int64_t)p.kvheads * D + (int64_t)local * D;
-#pragma unroll
-  for (int which = 0; which < 2; ++which) {
-    uint8_t* codes = static_cast<uint8_t*>(which ? p.v_cache : p.k_cache) + data;
-    uint8_t* scales = static_cast<uint8_t*>(which ? p.v_scales : p.k_scales) + sfo;
-    const float g = which ? vg : kg;
-    if (which) {
-#pragma unroll
-      for (int i = 0; i < E2; ++i) {
-        x[i] = __bfloat162float(qkv[vbase + d0 + i]);
-        y[i] = __bfloat162float(qkv[vbase + HALF + d0 + i]);
-      }
-    }
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const float* v = half ? y : x;
-      const int dstart = half * HALF + d0;
-      float amax = 0.0f;
-#pragma unroll
-      for (int i = 0; i < E2; ++i) amax = fmaxf(amax, fabsf(v[i]));
-#pragma unroll
-      for (int d = 1; d < 16 / E2; d <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
-      const uint32_t code = f_to_e4m3(__fdiv_rn(amax, __fmul_rn(6.0f, g)));
-      const float scale = e4m3_to_f(code);
-      const float inverse = scale > 0.0f ? __fdiv_rn(1.0f, __fmul_rn(scale, g)) : 0.0f;
-      if ((dstart & 15) == 0) scales[dstart >> 4] = (uint8_t)code;
-      if constexpr (E2 == 1) {
-        const float mine = __fmul_rn(v[0], inverse);
-        const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
-        if ((lane & 1) == 0) codes[dstart >> 1] = (uint8_t)f2_to_e2m1x2(mine, other);
+      const int64_t co = pos * p.cos_row + d0 + i;
+      if (p.cos_float) {
+        cs[i] = static_cast<const float*>(p.cos_sin)[co];
+        sn[i] = static_cast<const float*>(p.cos_sin)[co + HALF];
       } else {
+        cs[i] = __bfloat162float(static_cast<const __nv_bfloat16*>(p.cos_sin)[co]);
+        sn[i] = __bfloat162float(static_cast<const __nv_bfloat16*>(p.cos_sin)[co + HALF]);
+      }
+      wq[0][i] = __fadd_rn(__bfloat162float(qw[d0 + i]), p.weight_offset);
+      wq[1][i] = __fadd_rn(__bfloat162float(qw[HALF + d0 + i]), p.weight_offset);
+      wk[0][i] = __fadd_rn(__bfloat162float(kw[d0 + i]), p.weight_offset);
+      wk[1][i] = __fadd_rn(__bfloat162float(kw[HALF + d0 + i]), p.weight_offset);
+    }
+  }
+  int64_t slot = -1;
+  if (row < p.slot_rows)
+    slot = p.slot_long ? static_cast<const int64_t*>(p.slots)[row] : static_cast<const int32_t*>(p.slots)[row];
+  for (int head = warp; head < p.qheads + p.kvheads; head += 8) {
+    const bool is_k = head >= p.qheads;
+    const int local = is_k ? head - p.qheads : head;
+    if (is_k && slot < 0) break;  // padding token (or past slot_rows): nothing to append
+    const int64_t base =
+        row * p.input_row + (is_k ? (int64_t)p.qheads * 2 * D + (int64_t)local * D : (int64_t)local * 2 * D);
+    float x[E2], y[E2];
 #pragma unroll
-        for (int i = 0; i < E2; i += 2)
-          codes[(dstart + i) >> 1] = (uint8_t)f2_to_e2m1x2(__fmul_rn(v[i], inverse), __fmul_rn(v[i + 1], inverse));
+    for (int i = 0; i < E2; ++i) {
+      x[i] = __bfloat162float(qkv[base + d0 + i]);
+      y[i] = __bfloat162float(qkv[base + HALF + d0 + i]);
+    }
+    float ss = __fmul_rn(x[0], x[0]);
+    ss = __fadd_rn(ss, __fmul_rn(y[0], y[0]));
+#pragma unroll
+    for (int i = 1; i < E2; ++i) {
+      ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));
+      ss = __fadd_rn(ss, __fmul_rn(y[i], y[i]));
+    }
+    ss = warp_sum_butterfly(ss);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), p.eps)));
+    const float* w0 = is_k ? wk[0] : wq[0];
+    const float* w1 = is_k ? wk[1] : wq[1];
+#pragma unroll
+    for (int i = 0; i < E2; ++i) {
+      const float a = bf16r(__fmul_rn(__fmul_rn(x[i], inv), w0[i]));
+      const float b = bf16r(__fmul_rn(__fmul_rn(y[i], inv), w1[i]));
+      x[i] = bf16r(__fsub_rn(__fmul_rn(a, cs[i]), __fmul_rn(b, sn[i])));
+      y[i] = bf16r(__fadd_rn(__fmul_rn(b, cs[i]), __fmul_rn(a, sn[i])));
+    }
+    if (!is_k) {
+      __nv_bfloat16* q = static_cast<__nv_bfloat16*>(p.q) + row * p.q_row + (int64_t)local * D;
+#pragma unroll
+      for (int i = 0; i < E2; ++i) {
+        q[d0 + i] = __float2bfloat16_rn(x[i]);
+        q[HALF + d0 + i] = __float2bfloat16_rn(y[i]);
+      }
+      if (p.gate) {
+        __nv_bfloat16* g = static_cast<__nv_bfloat16*>(p.gate) + row * p.gate_row + (int64_t)local * D;
+#pragma unroll
+        for (int i = 0; i < E2; ++i) {
+          g[d0 + i] = qkv[base + D + d0 + i];
+          g[HALF + d0 + i] = qkv[base + D + HALF + d0 + i];
+        }
+      }
+      continue;
+    }
+    if (slot >= (int64_t)p.pages * p.page_size) {
+      if (lane == 0) report(p.status, kStatusBadSlot);
+      break;
+    }
+    const float kg = *p.k_global, vg = *p.v_global;
+    if (!(isfinite(kg) && kg > 0.0f && isfinite(vg) && vg > 0.0f)) {
+      if (lane == 0) report(p.status, kStatusBadKvScale);
+      break;
+    }
+    const int64_t page = slot / p.page_size, entry = slot % p.page_size;
+    const int64_t data = page * p.data_page + entry * p.data_row + (int64_t)local * p.data_head;
+    const int64_t sfo = page * p.sf_page + entry * p.sf_row + (int64_t)local * p.sf_head;
+    const int64_t vbase = row * p.input_row + (int64_t)p.qheads * 2 * D + (int64_t)p.kvheads * D + (int64_t)local * D;
+#pragma unroll
+    for (int which = 0; which < 2; ++which) {
+      uint8_t* codes = static_cast<uint8_t*>(which ? p.v_cache : p.k_cache) + data;
+      uint8_t* scales = static_cast<uint8_t*>(which ? p.v_scales : p.k_scales) + sfo;
+      const float g = which ? vg : kg;
+      if (which) {
+#pragma unroll
+        for (int i = 0; i < E2; ++i) {
+          x[i] = __bfloat162float(qkv[vbase + d0 + i]);
+          y[i] = __bfloat162float(qkv[vbase + HALF + d0 + i]);
+        }
+      }
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const float* v = half ? y : x;
+        const int dstart = half * HALF + d0;
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < E2; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+        for (int d = 1; d < 16 / E2; d <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
+        const uint32_t code = f_to_e4m3(__fdiv_rn(amax, __fmul_rn(6.0f, g)));
+        const float scale = e4m3_to_f(code);
+        const float inverse = scale > 0.0f ? __fdiv_rn(1.0f, __fmul_rn(scale, g)) : 0.0f;
+        if ((dstart & 15) == 0) scales[dstart >> 4] = (uint8_t)code;
+        if constexpr (E2 == 1) {
+          const float mine = __fmul_rn(v[0], inverse);
+          const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
+          if ((lane & 1) == 0) codes[dstart >> 1] = (uint8_t)f2_to_e2m1x2(mine, other);
+        } else {
+#pragma unroll
+          for (int i = 0; i < E2; i += 2)
+            codes[(dstart + i) >> 1] = (uint8_t)f2_to_e2m1x2(__fmul_rn(v[i], inverse), __fmul_rn(v[i + 1], inverse));
+        }
       }
     }
   }
 }
 
-// One CTA per row, thread t owns 16 consecutive columns.
 // The gate of column c sits at gate + row * gate_row + (c / head_dim) *
 // head_stride + c % head_dim: a compact [rows, cols] gate (head_dim = cols),
 // or the gate halves read in place from the QKV projection's per-head
@@ -264,9 +277,13 @@ __global__ void gate_fp8_kernel(const __nv_bfloat16* __restrict__ out, const __n
     load16_bf16(out + row * out_row + 16 * t, o);
     load16_bf16(gate + row * gate_row + (int64_t)(16 * t / head_dim) * head_stride + (16 * t) % head_dim, g);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      v[j] = bf16r(__fmul_rn(o[j], bf16r(sigmoid_f(g[j]))));
-      amax = fmaxf(amax, fabsf(v[j]));
+    for (int j = 0; j < 16; j += 2) {
+      float s0 = sigmoid_f(g[j]), s1 = sigmoid_f(g[j + 1]);
+      bf16r2(s0, s1);
+      float v0 = __fmul_rn(o[j], s0), v1 = __fmul_rn(o[j + 1], s1);
+      bf16r2(v0, v1);
+      v[j] = v0, v[j + 1] = v1;
+      amax = fmaxf(amax, fmaxf(fabsf(v0), fabsf(v1)));
     }
   }
   amax = block_max(amax, scratch);
@@ -275,11 +292,9 @@ __global__ void gate_fp8_kernel(const __nv_bfloat16* __restrict__ out, const __n
   if (!active) return;
   uint32_t w[4];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    w[k] = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) w[k] |= f_to_e4m3(__fdiv_rn(v[4 * k + j], scale)) << (8 * j);
-  }
+  for (int k = 0; k < 4; ++k)
+    w[k] = f2_to_e4m3x2(__fdiv_rn(v[4 * k], scale), __fdiv_rn(v[4 * k + 1], scale)) |
+           (f2_to_e4m3x2(__fdiv_rn(v[4 * k + 2], scale), __fdiv_rn(v[4 * k + 3], scale)) << 16);
   reinterpret_cast<uint4*>(fp8 + row * fp8_row)[t] = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
@@ -517,7 +532,7 @@ int qi_qk_rope_kv_append(const QiFront* p, cudaStream_t stream) {
                            !p->k_scales || !p->v_scales))
     return (int)cudaErrorInvalidValue;
   if (p->slot_rows > p->rows) return (int)cudaErrorInvalidValue;
-  const dim3 grid(p->rows, (p->qheads + p->kvheads + 7) / 8);
+  const dim3 grid(p->rows);
   switch (p->head_dim) {
     case 64: front_kernel<1><<<grid, 256, 0, stream>>>(*p); break;
     case 128: front_kernel<2><<<grid, 256, 0, stream>>>(*p); break;
