@@ -63,6 +63,13 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-kernel-timing", action="store_true")
     p.add_argument("--layers", type=int, default=None, help="override layer count (must split into 2N stages)")
+    p.add_argument("--workload", choices=("prefill", "decode"), default="prefill",
+                   help="prefill: the folded-VPP bank (default); decode: the bucket decode attention over the "
+                        "paged NVFP4 cache (one query token per request, 1 GPU)")
+    p.add_argument("--decode-batch", type=int, default=32)
+    p.add_argument("--decode-context", type=int, default=32768)
+    p.add_argument("--decode-mode", choices=("auto", "native", "persistent", "aligned"), default="persistent",
+                   help="task mode (auto: the route rule of the reference; persistent measured best here)")
     return p.parse_args()
 
 
@@ -405,8 +412,160 @@ def run_ours(args):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# Decode workload: bucket decode attention (one layer's attention of a decode
+# step) over the paged NVFP4 cache
+# ---------------------------------------------------------------------------
+DECODE_METRIC = "bucket decode attention KV read rate (GB/s) over the paged NVFP4 cache, 64/8 heads, D 128"
+
+
+def decode_bytes(batch, context, kvheads=8, head_dim=128):
+    """Algorithmic bytes of one call: K and V codes + scales of every key."""
+    return batch * context * kvheads * 2 * (head_dim // 2 + head_dim // 16)
+
+
+def decode_cpu_sample(threads, context):
+    """The oracle's decode attention on one request x ``context`` keys x 8 KV
+    heads (bounded sample), as a KV read rate."""
+    import numpy as np
+    import torch
+    from oracle import decode as OD
+
+    torch.set_num_threads(threads)
+    rng = np.random.default_rng(5)
+    hq, hkv, d = 64, 8, 128
+    q = rng.standard_normal((1, hq, d)).astype(np.float32)
+    k = [rng.standard_normal((context, hkv, d)).astype(np.float32)]
+    v = [rng.standard_normal((context, hkv, d)).astype(np.float32)]
+    plan = OD.task_plan([context], ctas=1, table_width=(context + 15) // 16, page_size=16)
+    t0 = time.perf_counter()
+    OD.decode_attention(q, k, v, [context], plan, softmax_scale=d ** -0.5, k_global=1.0, v_global=1.0)
+    dt = time.perf_counter() - t0
+    return dict(value=decode_bytes(1, context) / dt / 1e9, unit="GB/s", cores=threads, kind="port",
+                sample=f"oracle decode attention, 1 request x {context} keys x 8 KV heads ({dt:.1f} s)")
+
+
+def run_decode(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    sample_ctx = min(args.decode_context, 16384)
+    config = dict(workload=f"decode attention, {args.decode_batch} requests x {args.decode_context} keys, "
+                           f"64/8 heads, D 128, page 16", batch=args.decode_batch, context=args.decode_context,
+                  l2="KV larger than L2" if decode_bytes(args.decode_batch, args.decode_context) > 126e6
+                  else "KV smaller than L2; L2 flushed between calls")
+    if args.impl == "reference":
+        cpu = decode_cpu_sample(threads, sample_ctx)
+        line = dict(metric=DECODE_METRIC, value=cpu["value"], unit="GB/s", n_gpus=1, steps=args.steps,
+                    warmup=args.warmup, ms_per_step=decode_bytes(args.decode_batch, args.decode_context)
+                    / (cpu["value"] * 1e9) * 1e3, higher_is_better=True, scaling="weak", vs_baseline=None,
+                    dtype="f32", data="synthetic", impl="reference", config=config, cpu_baseline=cpu,
+                    e2e=dict(value=cpu["value"], unit="GB/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+        print(json.dumps(line), flush=True)
+        return 0
+    import torch
+
+    __graft_entry__.load_package()
+    from qwen_infra_b200 import decode as D
+    from qwen_infra_b200 import kernels as K
+    from qwen_infra_b200.kernels import PagedKV
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    b, ctx, hq, hkv, ps = args.decode_batch, args.decode_context, 64, 8, 16
+    width = (ctx + ps - 1) // ps
+    kv = PagedKV(b * width, ps, hkv, 128, dev)
+    gen = torch.Generator(device=dev).manual_seed(11)
+    for t in (kv.k, kv.v):
+        t.copy_(torch.randint(0, 256, t.shape, generator=gen, device=dev, dtype=torch.int32).to(torch.uint8))
+    for t in (kv.ks, kv.vs):
+        t.fill_(0x30)  # e4m3 0.5
+    table = torch.randperm(b * width, generator=gen, device=dev).to(torch.int32).view(b, width)
+    lengths_host = [ctx] * b
+    lengths = torch.tensor(lengths_host, dtype=torch.int32, device=dev)
+    q = torch.randn(b, hq, 128, generator=gen, device=dev).to(torch.bfloat16)
+    kg = torch.tensor([1.0], device=dev)
+    vg = torch.tensor([1.0], device=dev)
+    ws = D.Workspace(b, qheads=hq, kvheads=hkv, device=dev)
+    route = args.decode_mode if args.decode_mode != "auto" else D.route(lengths_host, table_width=width,
+                                                                          sm_count=ws.ctas, page_size=ps)
+    ws.bind(q, kv, table, lengths, k_global=kg, v_global=vg, cyclic=route == "native", aligned=route == "aligned",
+            persistent=route == "persistent")
+    nbytes = decode_bytes(b, ctx)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if nbytes <= 126e6 else None
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(3, args.warmup)):
+        ws.run()
+    torch.cuda.synchronize()
+    steps = max(args.steps, 20)
+    counter = K.LaunchProfile(timing=False)
+    K.PROFILE = counter
+    sampler = ClockSampler(REPO / "gpurun_out" / "clocks_decode.csv")
+    sampler.start()
+    times = []
+    for _ in range(steps):
+        if flush is not None:
+            flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        ws.run()  # plan (assign) + attention, as a decode step runs them
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    clocks = sampler.stop()
+    K.PROFILE = None
+    launches = counter.launches / steps
+    ms = statistics.median(times)
+    # kernel alone (no plan), the roofline's launch
+    kt = []
+    for _ in range(steps):
+        if flush is not None:
+            flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        ws.compute()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        kt.append(e0.elapsed_time(e1))
+    kms = statistics.median(kt)
+    # e2e: q copied from pinned host memory, output read back, every step
+    q_host = q.cpu().pin_memory()
+    out_host = torch.empty(ws.output.shape, dtype=torch.bfloat16).pin_memory()
+    et = []
+    for _ in range(steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        q.copy_(q_host, non_blocking=True)
+        ws.run()
+        out_host.copy_(ws.output, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        et.append(e0.elapsed_time(e1))
+    ems = statistics.median(et)
+    peaks, peak_kind = load_peaks()
+    achieved = nbytes / (kms / 1e3) / 1e9
+    cpu = decode_cpu_sample(os.cpu_count() or 1, sample_ctx) if not args.no_cpu_baseline else None
+    line = dict(
+        metric=DECODE_METRIC, value=nbytes / (ms / 1e3) / 1e9, unit="GB/s", n_gpus=1, steps=steps,
+        warmup=max(3, args.warmup), ms_per_step=ms, higher_is_better=True, scaling="weak", vs_baseline=None,
+        dtype="nvfp4 KV (e2m1 x e4m3/16) -> f16 tcgen05, fp32 softmax", data="synthetic (random codes, seeded q)",
+        config=dict(config, route=route, ctas=ws.ctas, decode_tokens_per_s_per_layer=b / (ms / 1e3)),
+        roofline=dict(kernel="decode_attention", bound="hbm", achieved=achieved, peak=peaks["hbm_gbs"], unit="GB/s",
+                      frac=achieved / peaks["hbm_gbs"], peak_source=f"hbm_gbs ({peak_kind})", traffic=None),
+        gpu_launches=int(launches * steps), clocks=clocks,
+        e2e=dict(value=nbytes / (ems / 1e3) / 1e9, unit="GB/s", ms_per_step=ems,
+                 h2d_bytes_per_step=q.numel() * 2, d2h_bytes_per_step=out_host.numel() * 2),
+        cpu_baseline=cpu, kernel_ms=kms,
+    )
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse()
+    if args.workload == "decode":
+        return run_decode(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
