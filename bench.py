@@ -63,6 +63,8 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-kernel-timing", action="store_true")
     p.add_argument("--layers", type=int, default=None, help="override layer count (must split into 2N stages)")
+    p.add_argument("--kv-shadow", choices=("auto", "on", "off"), default="auto",
+                   help="keep each request's f16 K/V^T across its chunks (dequantise new tokens only)")
     p.add_argument("--workload", choices=("prefill", "decode"), default="prefill",
                    help="prefill: the folded-VPP bank (default); decode: the bucket decode attention over the "
                         "paged NVFP4 cache (one query token per request, 1 GPU)")
@@ -245,7 +247,7 @@ def run_ours(args):
                                     profile=args.profile)
     request_tokens = [args.prompt_tokens] * args.requests
     runner = FoldedRank(shape, rank, world, dev, request_tokens, args.chunk_size, transport=transport,
-                        profile=args.profile)
+                        profile=args.profile, kv_shadow={"auto": None, "on": True, "off": False}[args.kv_shadow])
     gen = torch.Generator(device=dev).manual_seed(4321)
     embeds = [torch.randn(t, shape.hidden, generator=gen, device=dev).to(torch.bfloat16) for t in request_tokens] \
         if rank == 0 else None

@@ -171,6 +171,13 @@ typedef struct QiKvView {
  * values are the exact e2m1 x e4m3 products (global multipliers not applied). */
 int qi_kv_dequant(const QiKvView* kv, const int32_t* block_table, int tokens, void* k_out, void* vt_out,
                   int64_t vt_row, cudaStream_t stream);
+/* Tokens [first, tokens) only (first % 64 == 0), into K buffers of
+ * k_capacity >= tokens rows per head (k_out f16 [Hkv, k_capacity, D]): a
+ * caller that keeps the f16 K / V^T of a request across its chunks
+ * dequantises each chunk's new tokens once (tokens past `tokens` in the last
+ * 64-token group are written as zeros). */
+int qi_kv_dequant_range(const QiKvView* kv, const int32_t* block_table, int first, int tokens, void* k_out,
+                        int64_t k_capacity, void* vt_out, int64_t vt_row, cudaStream_t stream);
 
 typedef struct QiAttention {
   const void* q;         /* bf16 [rows, Hq*D] (row stride q_row elements) */

@@ -95,6 +95,7 @@ EXPORTS = {
     "qi_gemm": ([ct.POINTER(QiGemm), _vp], _i32),
     "qi_gemm_resources": ([ct.POINTER(_i32)], _i32),
     "qi_kv_dequant": ([ct.POINTER(QiKvView), _vp, _i32, _vp, _vp, _i64, _vp], _i32),
+    "qi_kv_dequant_range": ([ct.POINTER(QiKvView), _vp, _i32, _i32, _vp, _i64, _vp, _i64, _vp], _i32),
     "qi_swiglu_nvfp4": ([_vp, _i64, _i32, _i32, _vp, _vp, _i64, _vp, _vp], _i32),
     "qi_lm_head_argmax": ([_vp, _i64, _i32, _i32, _vp, _i32, _vp, _vp, _vp, _vp], _i32),
     "qi_lm_head_workspace_bytes": ([], _i32),

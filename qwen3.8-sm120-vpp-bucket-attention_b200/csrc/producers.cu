@@ -375,7 +375,8 @@ __global__ void fp8_rows_kernel(const float* __restrict__ w, int k, uint8_t* __r
 template <int D>
 __global__ void __launch_bounds__(256) kv_dequant_kernel(const uint8_t* __restrict__ kc, const uint8_t* __restrict__ vc,
                                                          const uint8_t* __restrict__ ksf, const uint8_t* __restrict__ vsf,
-                                                         const int32_t* __restrict__ block_table, int tokens, int page_size,
+                                                         const int32_t* __restrict__ block_table, int first, int tokens,
+                                                         int page_size,
                                                          int64_t data_page, int64_t data_row, int64_t data_head,
                                                          int64_t sf_page, int64_t sf_row, int64_t sf_head,
                                                          __half* __restrict__ k_out, __half* __restrict__ vt_out,
@@ -393,7 +394,7 @@ __global__ void __launch_bounds__(256) kv_dequant_kernel(const uint8_t* __restri
   }
   __syncthreads();
   const int head = blockIdx.y;
-  const int t0 = blockIdx.x * 64;
+  const int t0 = first + blockIdx.x * 64;
   const int part = threadIdx.x % PARTS;
   for (int tl = threadIdx.x / PARTS; tl < 64; tl += TOK) {
     const int tok = t0 + tl;
@@ -671,10 +672,11 @@ int qi_fp8_quantize_rows(const float* w, int rows, int k, void* q, float* scales
   return (int)cudaPeekAtLastError();
 }
 
-int qi_kv_dequant(const QiKvView* kv, const int32_t* block_table, int tokens, void* k_out, void* vt_out,
-                  int64_t vt_row, cudaStream_t stream) {
+int qi_kv_dequant_range(const QiKvView* kv, const int32_t* block_table, int first, int tokens, void* k_out,
+                        int64_t k_capacity, void* vt_out, int64_t vt_row, cudaStream_t stream) {
   QI_BIND(stream, k_out);
-  if (!kv || !block_table || tokens < 1 || !k_out || !vt_out || vt_row < tokens || vt_row % 64)
+  if (!kv || !block_table || tokens < 1 || first < 0 || first % 64 || first >= tokens || !k_out || !vt_out ||
+      k_capacity < tokens || vt_row < tokens || vt_row % 64)
     return (int)cudaErrorInvalidValue;
   if (!kv->k_cache || !kv->v_cache || !kv->k_scales || !kv->v_scales || kv->kvheads < 1 || kv->page_size < 1)
     return (int)cudaErrorInvalidValue;
@@ -684,13 +686,13 @@ int qi_kv_dequant(const QiKvView* kv, const int32_t* block_table, int tokens, vo
       (reinterpret_cast<uintptr_t>(kv->v_scales) & 1) || kv->sf_page % 2 || kv->sf_row % 2 || kv->sf_head % 2 ||
       !aligned16(k_out) || !aligned16(vt_out))
     return (int)cudaErrorInvalidValue;
-  const dim3 grid((tokens + 63) / 64, kv->kvheads);
-  const int64_t ks = (int64_t)tokens * kv->head_dim, vs = (int64_t)kv->head_dim * vt_row;
+  const dim3 grid((tokens - first + 63) / 64, kv->kvheads);
+  const int64_t ks = k_capacity * kv->head_dim, vs = (int64_t)kv->head_dim * vt_row;
 #define QI_KVD(DD)                                                                                                  \
   kv_dequant_kernel<DD><<<grid, 256, 0, stream>>>(                                                                  \
       static_cast<const uint8_t*>(kv->k_cache), static_cast<const uint8_t*>(kv->v_cache),                          \
-      static_cast<const uint8_t*>(kv->k_scales), static_cast<const uint8_t*>(kv->v_scales), block_table, tokens,   \
-      kv->page_size, kv->data_page, kv->data_row, kv->data_head, kv->sf_page, kv->sf_row, kv->sf_head,            \
+      static_cast<const uint8_t*>(kv->k_scales), static_cast<const uint8_t*>(kv->v_scales), block_table, first,    \
+      tokens, kv->page_size, kv->data_page, kv->data_row, kv->data_head, kv->sf_page, kv->sf_row, kv->sf_head,     \
       static_cast<__half*>(k_out), static_cast<__half*>(vt_out), ks, vs, vt_row)
   switch (kv->head_dim) {
     case 64: QI_KVD(64); break;
@@ -699,6 +701,11 @@ int qi_kv_dequant(const QiKvView* kv, const int32_t* block_table, int tokens, vo
   }
 #undef QI_KVD
   return (int)cudaPeekAtLastError();
+}
+
+int qi_kv_dequant(const QiKvView* kv, const int32_t* block_table, int tokens, void* k_out, void* vt_out,
+                  int64_t vt_row, cudaStream_t stream) {
+  return qi_kv_dequant_range(kv, block_table, 0, tokens, k_out, tokens, vt_out, vt_row, stream);
 }
 
 int qi_convert_probe(const float* in, void* e2m1_pairs, void* e4m3, float* ex, int n, cudaStream_t stream) {

@@ -308,19 +308,26 @@ def gemm_e4m3(a, b, *, m, n, k, row_scale=None, col_scale=None, alpha_value=1.0,
     return out
 
 
-def kv_dequant(kv, block_table, tokens, *, k_out=None, vt_out=None):
-    """Paged NVFP4 KV of one request -> f16 K [Hkv, tokens, D] and V^T
-    [Hkv, D, vt_row] (vt_row = tokens rounded up to 64), exact e2m1 x e4m3."""
+def kv_dequant(kv, block_table, tokens, *, first=0, k_out=None, vt_out=None):
+    """Paged NVFP4 KV of one request -> f16 K [Hkv, capacity, D] and V^T
+    [Hkv, D, vt_row] (exact e2m1 x e4m3) for tokens [first, tokens); ``first``
+    a multiple of 64 (0: the whole history).  Without outputs, buffers of
+    exactly ``tokens`` (vt_row rounded up to 64) are allocated."""
     _cuda(block_table)
-    vt_row = (tokens + 63) // 64 * 64
     d = kv.head_dim
     if k_out is None:
         k_out = torch.empty((kv.kvheads, tokens, d), dtype=torch.float16, device=kv.k.device)
     if vt_out is None:
-        vt_out = torch.empty((kv.kvheads, d, vt_row), dtype=torch.float16, device=kv.k.device)
+        vt_out = torch.empty((kv.kvheads, d, (tokens + 63) // 64 * 64), dtype=torch.float16, device=kv.k.device)
+    if k_out.shape[0] != kv.kvheads or k_out.shape[2] != d or not k_out.is_contiguous() \
+            or vt_out.shape[:2] != (kv.kvheads, d) or not vt_out.is_contiguous():
+        raise ValueError("k_out [Hkv, capacity, D] and vt_out [Hkv, D, vt_row], contiguous")
     view = kv.view()
-    N.check(_run("kv_dequant", tokens * kv.kvheads * (d + d // 8 + 4 * d), "B", kv.k.device, lambda: N.lib().qi_kv_dequant(ct.byref(view), _ptr(block_table), tokens, _ptr(k_out), _ptr(vt_out), vt_row,
-                                  _stream(kv.k.device))), "qi_kv_dequant")
+    n = tokens - first
+    N.check(_run("kv_dequant", n * kv.kvheads * (d + d // 8 + 4 * d), "B", kv.k.device,
+                 lambda: N.lib().qi_kv_dequant_range(ct.byref(view), _ptr(block_table), first, tokens, _ptr(k_out),
+                                                     k_out.shape[1], _ptr(vt_out), vt_out.shape[2],
+                                                     _stream(kv.k.device))), "qi_kv_dequant_range")
     return k_out, vt_out
 
 
