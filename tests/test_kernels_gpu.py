@@ -329,6 +329,25 @@ def test_kv_dequant_exact(K, tokens, d):
     assert np.array_equal(vt.float().cpu().numpy()[:, :, :tokens], v_ref.transpose(1, 2, 0))
 
 
+def test_kv_dequant_range_by_chunks_equals_whole_history(K):
+    """Chunks of 700 tokens dequantised one after another into buffers sized
+    for the whole request equal the whole-history dequantisation; tokens past
+    the current length stay zero."""
+    tokens, kvh, d, cap = 2500, 8, 128, 2600
+    kvc, table = _kv_fixture(K, tokens, kvh, d, tokens)
+    tt = torch.from_numpy(table).to(DEV)
+    full_k, full_vt = K.kv_dequant(kvc, tt, tokens)
+    kd = torch.zeros(kvh, cap, d, dtype=torch.float16, device=DEV)
+    vt = torch.zeros(kvh, d, (cap + 63) // 64 * 64, dtype=torch.float16, device=DEV)
+    for end in (700, 1400, 2100, 2500):
+        hist = end - 700 if end != 2500 else 2100
+        K.kv_dequant(kvc, tt, end, first=hist // 64 * 64, k_out=kd, vt_out=vt)
+        torch.cuda.synchronize()
+        assert torch.equal(kd[:, :end], full_k[:, :end])
+        assert torch.equal(vt[:, :, :end], full_vt[:, :, :end])
+        assert not kd[:, end:].any() and not vt[:, :, end:].any()
+
+
 @pytest.mark.parametrize("split", [True, False])
 @pytest.mark.parametrize("rows,history,qh,kvh,d", [(128, 0, 16, 4, 64), (200, 300, 16, 4, 64),
                                                    (512, 0, 64, 8, 128), (77, 1500, 64, 8, 128),
