@@ -125,3 +125,89 @@ def test_bank_output_tokens_are_the_greedy_samples_of_its_final_hidden():
     _, want = P.lm_head_argmax(last.float().cpu().numpy(), runner.model.lm_head.float().cpu().numpy())
     assert got == want.tolist()
     assert all(0 <= t < M.TINY.vocab for t in got)
+
+
+def test_27b_shape_layer_every_stage_and_end_to_end():
+    """One 27B-shaped decoder layer (H5120, 64/8 heads, D128, I17408, page 16)
+    on two 2048-row chunks of one request (history 0 and 2048), teacher-forced
+    with the oracle's KV history.
+
+    Stage by stage, each kernel's output is compared with the oracle applied
+    to the GPU's own input of that stage: the quantised bytes (norm packs,
+    K/V codes and scales, FP8 gate output, SwiGLU codes) bit-exact or all but
+    a few codes, the fp32-accumulated products (QKV, O, down) within 1e-3, the
+    attention within 5e-3 (f16 P on the GPU, fp32 P in the oracle, bf16
+    output).  End to end the layer is compared with the oracle's own chain:
+    every requantisation (bf16 output, FP8, two NVFP4 packs) turns the last-ulp
+    differences into whole-step code flips, and the oracle itself computed with
+    fp32 instead of fp64 GEMM accumulation differs by 3.4e-2 (relative L2 of
+    h + r) at this shape, so the end-to-end bar is 1e-1 here (the tiny
+    configuration keeps 2e-2)."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from oracle import formats as F
+    from qwen_infra_b200.vpp import model as M
+
+    dev = torch.device("cuda:0")
+    tokens, chunk = 4096, 2048
+    s = OM.QWEN27B
+    # host-seeded weights, as the oracle builds them (not the on-device init)
+    stage = M.StageModel(M.QWEN27B, [0], dev, max_rows=chunk, request_tokens=[tokens], on_device_init=False)
+    oracle = OM.OracleModel(s, [0], tokens)
+    w, dq, ws = oracle.w[0], oracle.deq[0], stage.ws
+    x = torch.randn(tokens, s.hidden, generator=torch.Generator().manual_seed(77)).to(torch.bfloat16)
+    r = torch.randn(tokens, s.hidden, generator=torch.Generator().manual_seed(78)).to(torch.bfloat16)
+    for start in range(0, tokens, chunk):
+        ctx = stage.chunk_context(0, start, chunk)
+        kv_g, kv_o = stage.kv[0], oracle.kv[0]
+        for dst, src in ((kv_g.k, kv_o.k), (kv_g.v, kv_o.v), (kv_g.ks, kv_o.ks), (kv_g.vs, kv_o.vs)):
+            dst.copy_(torch.from_numpy(src))
+        hist_kv = [t.copy() for t in (kv_o.k, kv_o.v, kv_o.ks, kv_o.vs)]
+        h_in, r_in = x[start:start + chunk], r[start:start + chunk]
+        ho = torch.empty_like(h_in, device=dev)
+        ro = torch.empty_like(h_in, device=dev)
+        stage.layer_forward(0, h_in.to(dev), r_in.to(dev), ctx, ho, ro)
+        torch.cuda.synchronize()
+        # --- stage by stage, each on the GPU's own input ---------------------
+        q_in, sf_in, res1 = P.norm_pack(h_in.float().numpy(), r_in.float().numpy(), w["ln_in"],
+                                        OM.ACT_GLOBAL_NORM, s.eps)
+        assert np.array_equal(ws.q_in[:chunk].cpu().numpy(), q_in)
+        assert np.array_equal(ws.res1[:chunk].float().cpu().numpy(), res1)
+        a = F.nvfp4_dequant(q_in, sf_in, chunk, s.hidden, OM.ACT_GLOBAL_NORM)
+        qkv_g = ws.qkv[:chunk].float().cpu().numpy()
+        assert _rel_l2(qkv_g, F.bf16_round(OM._mm(a, dq["qkv"]))) < 1e-3
+        kvc = OM.KVCache(s, oracle.pages)
+        kvc.k, kvc.v, kvc.ks, kvc.vs = hist_kv
+        positions = np.arange(start, start + chunk)
+        q, gate = P.qk_rope_append(qkv_g, positions, w["q_norm"], w["k_norm"], oracle.rope, positions,
+                                   OM.KV_GLOBAL_K, OM.KV_GLOBAL_V, kvc.k, kvc.v, kvc.ks, kvc.vs, qheads=s.qheads,
+                                   kvheads=s.kvheads, head_dim=s.head_dim, page_size=s.page_size, eps=s.eps)
+        assert np.array_equal(ws.q[:chunk].float().cpu().numpy(), q)
+        for got, want in ((kv_g.k, kvc.k), (kv_g.v, kvc.v), (kv_g.ks, kvc.ks), (kv_g.vs, kvc.vs)):
+            assert np.array_equal(got.cpu().numpy(), want)
+        kd, vd = kvc.gather(oracle.block_table, start + chunk, s, OM.KV_GLOBAL_K, OM.KV_GLOBAL_V)
+        att_g = ws.att[:chunk].float().cpu().numpy()
+        assert _rel_l2(att_g, F.bf16_round(OM.attention_exact(q, kd, vd, start, s))) < 5e-3
+        a8, s8 = P.gate_fp8(att_g, gate)
+        assert np.array_equal(ws.a8[:chunk].cpu().numpy(), a8)
+        assert np.array_equal(ws.s8[:chunk].cpu().numpy(), s8)
+        o_g = ws.o[:chunk].float().cpu().numpy()
+        assert _rel_l2(o_g, F.bf16_round(OM._mm((F.e4m3_decode(a8) * s8[:, None]).astype(np.float32),
+                                                dq["o"]))) < 1e-3
+        q_m, sf_m, res2 = P.norm_pack(o_g, res1, w["ln_post"], OM.ACT_GLOBAL_NORM, s.eps)
+        assert np.array_equal(ws.q_m[:chunk].cpu().numpy(), q_m)
+        assert np.array_equal(ro.float().cpu().numpy(), res2)
+        am = F.nvfp4_dequant(q_m, sf_m, chunk, s.hidden, OM.ACT_GLOBAL_NORM)
+        gu = OM._mm(am, dq["gate_up"]).reshape(chunk, s.intermediate // 128, 2, 128)
+        q_act, sf_act, _ = P.swiglu_nvfp4(gu[:, :, 0, :].reshape(chunk, s.intermediate),
+                                          gu[:, :, 1, :].reshape(chunk, s.intermediate), 1.0, OM.ACT_GLOBAL_DOWN)
+        assert (ws.act_q[:chunk].cpu().numpy() == q_act).mean() > 0.9999  # a few boundary codes flip
+        act_g = F.nvfp4_dequant(ws.act_q[:chunk].cpu().numpy(), ws.act_sf.cpu().numpy(), chunk, s.intermediate,
+                                OM.ACT_GLOBAL_DOWN)
+        hg_np = ho.float().cpu().numpy()
+        assert _rel_l2(hg_np, F.bf16_round(OM._mm(act_g, dq["down"]))) < 1e-3
+        # --- end to end against the oracle's own chain ----------------------
+        h_o, r_o = oracle.layer(0, h_in.float().numpy(), r_in.float().numpy(), start)
+        assert _rel_l2(hg_np + res2, h_o + r_o) < 1e-1
+        assert _rel_l2(res2, r_o) < 2e-2
+    stage.check_status()
