@@ -235,7 +235,7 @@ typedef struct QiDecodeBucket { int32_t begin, end; } QiDecodeBucket;           
 
 typedef struct QiDecode {
   const void* q;                 /* bf16 [batch, qheads, 128], 16-byte aligned */
-  QiKvView kv;                   /* head_dim 128; code strides % 16, scale strides % 8 */
+  QiKvView kv;                   /* head_dim 128, power-of-two page_size; code base and strides % 32, scale % 8 */
   const int32_t* block_table;    /* [batch, table_width] page ids */
   const int32_t* lengths;        /* [batch] keys per request, 0 .. table_width * page_size */
   QiDecodeTask* tasks;           /* [ctas + batch - 1]  plan, written by qi_decode_assign */
@@ -258,8 +258,10 @@ typedef struct QiDecode {
 
 int qi_decode_assign(const QiDecode* p, cudaStream_t stream);
 int qi_decode_attention(const QiDecode* p, cudaStream_t stream);
-/* values[8]: sizeof(QiDecode), registers, shared bytes, local bytes, resident
- * CTAs per SM, sizeof(QiDecodeTask), sizeof(QiDecodeRange), sizeof(QiDecodeBucket). */
+/* values[10]: sizeof(QiDecode), registers, shared bytes, local bytes, resident
+ * CTAs per SM (groups of <= 8 query heads per KV head), sizeof(QiDecodeTask),
+ * sizeof(QiDecodeRange), sizeof(QiDecodeBucket), registers and resident CTAs
+ * per SM of the kernel for groups of 9..16. */
 int qi_decode_resources(int* values);
 uint64_t qi_decode_scratch_bytes(int capacity, int kvheads);
 

@@ -16,7 +16,9 @@ Two parts:
 * ``decode_attention``: one query token per request against its paged NVFP4
   K/V (the same cache the prefill path appends to), softmax(q K^T s) V with the
   arithmetic of the CUDA kernel: K and V are the exact e2m1 x e4m3 products,
-  q is rounded to f16, keys run in blocks of 128 with a deferred running max
+  the query group is written as a sum of ``Q_TERMS`` NVFP4 terms (``q_terms``:
+  the kernel's S product runs block-scaled on the cached K codes), keys run in
+  blocks of 128 with a deferred running max
   (moved only when a score exceeds it by more than 2^8), P is rounded to f16
   for the PV product, the running sum takes the unrounded exponentials, and
   task partials combine by exp2(m_i - m) weights.  The
@@ -115,22 +117,64 @@ def _f16(x):
     return x.to(torch.float16).to(torch.float32)
 
 
+Q_TERMS = 4  # NVFP4 terms of the query group in the kernel's S product
+
+
+def _e2m1_codes_values(codes):
+    return F.e2m1_decode(codes).astype(f32)
+
+
+def q_terms(qh, terms=Q_TERMS):
+    """The query group [G, D] (bf16 values) as a sum of NVFP4 terms, as the
+    kernel builds its S operand: term t quantises the residual r_t per 16
+    elements with the power-of-two global g_t = 2^floor(log2(2688 / amax_t))
+    (amax over the group; 2688/amax clamped to [2^-100, 2^100]), scale =
+    e4m3(min(amax16 * g_t * (1/6), 448)), code = e2m1(r * (g_t / scale)), and
+    r_{t+1} = r_t - code * scale / g_t (each step one fp32 operation).
+    Returns [(code * scale [G, D] float32, 1 / g_t)] per term (a zero group
+    gives zero terms)."""
+    r = np.asarray(qh, dtype=f32).copy()
+    g_rows, d = r.shape
+    out = []
+    for _ in range(terms):
+        amax = f32(np.abs(r).max()) if r.size else f32(0)
+        if not amax > 0:
+            out.append((np.zeros_like(r), 0.0))
+            continue
+        y = min(max(f32(f32(2688.0) / amax), f32(2.0 ** -100)), f32(2.0 ** 100))
+        g = f32(2.0 ** int(np.floor(np.log2(np.float64(y)))))
+        ig = f32(1.0) / g
+        blk = r.reshape(g_rows, d // 16, 16)
+        am16 = np.abs(blk).max(axis=-1).astype(f32)
+        pre = np.minimum(((am16 * g).astype(f32) * f32(1.0 / 6.0)).astype(f32), f32(448.0))
+        scale = F.e4m3_decode(F.e4m3_encode(pre)).astype(f32)
+        inv = np.where(scale > 0, (g / np.where(scale > 0, scale, f32(1))).astype(f32), f32(0)).astype(f32)
+        cv = _e2m1_codes_values(F.e2m1_encode((blk * inv[:, :, None]).astype(f32)))
+        unscaled = (cv * scale[:, :, None]).astype(f32)
+        r = (blk - (unscaled * ig).astype(f32)).astype(f32).reshape(g_rows, d)
+        out.append((unscaled.reshape(g_rows, d), float(ig)))
+    return out
+
+
 MAX_LAG = 8.0  # log2 headroom of the deferred running maximum
 
 
-def _task_partial(qh, kh, vh, tiles, length, scale2):
+def _task_partial(terms, kh, vh, tiles, length, scale2):
     """(O [G, D] unnormalised, m [G] log2 domain, l [G]) of one task for one KV
     head.  The running maxima move (all heads at once, to the block maximum)
     only on the task's first block or when some score of a block exceeds its
     head's maximum by more than ``MAX_LAG``; otherwise P = exp2(s - m) <= 2^8."""
-    g = qh.shape[0]
+    g = terms[0][0].shape[0]
+    tq = [torch.from_numpy(t.astype(np.float64)) for t, _ in terms]
+    cg = [float(f32(f32(ig) * f32(scale2))) for _, ig in terms]
     m = torch.full((g,), float("-inf"))
     l = torch.zeros(g)
     o = torch.zeros(g, vh.shape[1])
     for t in tiles:
         for b0 in range(t * TILE, min(t * TILE + TILE, length), BLOCK):
             b1 = min(b0 + BLOCK, length)
-            s = (qh @ kh[b0:b1].T) * scale2  # [G, keys], log2 units
+            kb = kh[b0:b1].double()
+            s = sum((t @ kb.T) * c for t, c in zip(tq, cg)).float()  # [G, keys], log2 units
             if bool(torch.isinf(m).any()) or bool((s > m[:, None] + MAX_LAG).any()):
                 m_new = torch.maximum(m, s.max(dim=1).values)
                 alpha = torch.where(m == float("-inf"), torch.zeros_like(m), torch.exp2(m - m_new))
@@ -159,10 +203,10 @@ def decode_attention(q, k, v, lengths, plan, *, softmax_scale, k_global, v_globa
         vr = torch.from_numpy(np.ascontiguousarray(v[r], dtype=f32))
         hkv = kr.shape[1]
         grp = hq // hkv
-        qr = _f16(torch.from_numpy(np.ascontiguousarray(q[r], dtype=f32)))
+        qr = np.ascontiguousarray(q[r], dtype=f32)
         for h in range(hkv):
-            qh = qr[h * grp:(h + 1) * grp]
-            parts = [_task_partial(qh, kr[:, h], vr[:, h], plan_tiles(plan["tasks"][s]), n, scale2)
+            terms = q_terms(qr[h * grp:(h + 1) * grp])
+            parts = [_task_partial(terms, kr[:, h], vr[:, h], plan_tiles(plan["tasks"][s]), n, scale2)
                      for s in range(first, first + count)]
             mx = torch.stack([p[1] for p in parts]).max(dim=0).values
             o = torch.zeros(grp, d)

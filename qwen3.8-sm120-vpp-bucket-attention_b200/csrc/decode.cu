@@ -16,20 +16,25 @@
 // a key costs D/2 + D/16 bytes of K and as much of V per KV head, and the
 // group of G = Hq/Hkv query heads makes 4*G*D flops of it -- too many for the
 // CUDA cores at HBM speed, so both products run on tcgen05:
-//   S^T[keys, G] = K . Q^T : A = K from TMEM (each thread dequantises its own
-//                            key row in registers and stores it with
-//                            tcgen05.st), B = Q^T from shared memory;
-//   O^T[D, G]  += V^T . P^T: A = V from shared memory in its natural
-//                            [key][D] order, read MN-major (no transpose),
-//                            B = P (f16) from shared memory.
-// Keeping K out of shared memory keeps the shared-memory traffic per block
-// (V written and read, P, Q) below what the block's HBM bytes allow.  The
-// softmax runs in the log2 domain with a running max per head (CTA-wide
-// reductions through shared memory), P is rounded to f16 for the PV product
-// and the running sum takes the unrounded exponentials.  A request served by
-// several tasks writes unnormalised partials (O, m, l); the last task to
-// finish (per request and KV head) merges them in slot order, so the result
-// does not depend on the order the CTAs ran in.
+//   S^T[keys, 64] = K . Qt^T: kind::mxf4nvf4 straight on the cached K codes
+//                            (A, shared memory) and block scales (TMEM), with
+//                            the query group written as a sum of four NVFP4
+//                            terms (B: 4 terms x 16 heads); per head the four
+//                            term columns combine in registers with their
+//                            power-of-two global scales;
+//   O^T[D, G]  += V^T . P^T: A = V (dequantised to f16) from shared memory in
+//                            its natural [key][D] order, read MN-major (no
+//                            transpose), B = P (f16) from shared memory.
+// Two K = 64 block-scaled MMAs make S where the f16 form needs eight K = 16
+// ones.  Neither HBM nor the MMAs bound the kernel: each CTA's block is a
+// serial chain (load issue, V dequantisation, S, softmax, P, PV) and three
+// CTAs per SM overlap three chains.  The softmax
+// runs in the log2 domain with a running max per head (CTA-wide reductions
+// through shared memory), P is rounded to f16 for the PV product and the
+// running sum takes the unrounded exponentials.  A request served by several
+// tasks writes unnormalised partials (O, m, l); the last task to finish (per
+// request and KV head) merges them in slot order, so the result does not
+// depend on the order the CTAs ran in.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -52,16 +57,25 @@ constexpr int kMaxBatch = 32;
 constexpr int kMaxCtas = 340;
 constexpr float kMaxLag = 8.0f;  // log2 headroom of the deferred softmax maximum
 
-// TMEM columns (128 allocated): K block (f16 pairs), S^T, O^T.
-constexpr uint32_t kColK = 0, kColS = 64, kColO = 96, kTmemCols = 128;
+constexpr int kQTerms = 4;        // NVFP4 terms of the query group (B rows 16 t + j)
+
+// TMEM columns (128 allocated): S^T (4 terms x 16 heads), O^T, block scales
+// of K (A) and of the query terms (B), 4 columns per K = 64 MMA each.
+constexpr uint32_t kColS = 0, kColO = 64, kColSfa = 80, kColSfb = 88, kTmemCols = 128;
 
 // Shared memory (offsets from the 1024-aligned base).
 constexpr uint32_t kOffV = 0;                  // V block, MN-major SW128: 2 D-halves x 16 KB
 constexpr uint32_t kVHalf = 16384;
-constexpr uint32_t kOffQ = 32768;              // Q^T operand: 2 K-blocks x (16 rows x 128 B)
-constexpr uint32_t kOffP = kOffQ + 4096;       // P operand:   2 K-blocks x (16 rows x 128 B)
-constexpr uint32_t kOffRed = kOffP + 4096;     // float [4][16] reductions
-constexpr uint32_t kOffMisc = kOffRed + 4 * kMaxGroup * 4;
+// K codes and query terms share one SW128 region of 128-byte rows: row r
+// holds key r's 64 code bytes in its first half (16-byte chunks 0-3 before the
+// swizzle) and, for r < 64, query-term row r in its second half (chunks 4-7).
+constexpr uint32_t kOffK = 32768;
+constexpr uint32_t kQHalf = 64;                // byte offset of the query terms within a row
+constexpr uint32_t kOffP = kOffK + 16384;      // P operand:   2 K-blocks x (16 rows x 128 B)
+constexpr uint32_t kOffSfk = kOffP + 4096;     // K scales of the block, [key][8] bytes
+constexpr uint32_t kOffSfq = kOffSfk + 1024;   // query-term scales, [64 rows][8] bytes
+constexpr uint32_t kOffRed = kOffSfq + 512;    // float [4][16] reductions + [kQTerms][4] term maxima
+constexpr uint32_t kOffMisc = kOffRed + (4 * kMaxGroup + 4 * kQTerms) * 4;
 constexpr uint32_t kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
 
 // ---------------------------------------------------------------------------
@@ -185,38 +199,26 @@ __device__ __forceinline__ uint32_t splat_half(uint32_t pair, int sel) {
   return sel ? __byte_perm(pair, 0, 0x3232) : __byte_perm(pair, 0, 0x1010);
 }
 
-// One key row of 128 values (64 code bytes as 4 x uint4, 8 scale bytes as
-// uint2) -> 64 f16 pairs in element order; `half` selects values
-// [64 half, 64 half + 64) (32 pairs), so a caller can stream the row in two
-// halves and keep fewer registers live.
-__device__ __forceinline__ void dequant_half(const uint4* codes, uint2 scales, int half, uint32_t* pairs) {
-  const uint32_t sw = half ? scales.y : scales.x;  // four scale groups of this half
-  const uint32_t s01 = e4m3x2_to_f16x2(sw & 0xFFFF), s23 = e4m3x2_to_f16x2(sw >> 16);
-#pragma unroll
-  for (int c = 0; c < 2; ++c) {  // two uint4 = 32 bytes = 64 values per half
-    const uint4 q = codes[2 * half + c];
-    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const int group = c * 2 + (w >> 1);  // 16 values (2 words) per scale group
-      const uint32_t s2 = splat_half(group < 2 ? s01 : s23, group & 1);
-      uint32_t f[4];
-      e2m1x8_to_f16x8(words[w], f);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) pairs[c * 16 + w * 4 + i] = hmul2u(f[i], s2);
-    }
-  }
+// 32 lanes x 8 columns (register i -> column taddr + i).
+__device__ __forceinline__ void tmem_st8w(uint32_t taddr, const uint32_t* v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
+               "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
 }
-
-__device__ __forceinline__ void tmem_st32w(uint32_t taddr, const uint32_t* v) {
+// Loads without the wait (the caller issues tcgen05.wait::ld once for several).
+__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t* r) {
   asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
-      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
-      "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
-      "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
       : "memory");
+}
+__device__ __forceinline__ void tmem_ld8_async(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
 }
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   uint32_t r[16];
@@ -243,15 +245,6 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-// D (+)= A . B, A from tensor memory, B from shared memory.
-__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
-      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
-      : "memory");
-}
 // D (+)= A . B, both from shared memory.
 __device__ __forceinline__ void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
@@ -262,10 +255,12 @@ __device__ __forceinline__ void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint3
       : "memory");
 }
 
-// kind::f16, f16 A and B, fp32 accumulator, M = 128, N = 16; bit 15: A is
-// MN-major (V read in its natural [key][D] order).
-constexpr uint32_t kIdescS = (1u << 4) | ((uint32_t)(kMaxGroup >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-constexpr uint32_t kIdescO = kIdescS | (1u << 15);
+// S: kind::mxf4nvf4, M = 128 keys, N = 4 terms x 16 heads.  PV: kind::f16,
+// f16 A and B, fp32 accumulator, M = 128, N = 16, bit 15: A is MN-major (V
+// read in its natural [key][D] order).
+constexpr uint32_t kIdescS = idesc_nvfp4(kQTerms * kMaxGroup);
+constexpr uint32_t kIdescO =
+    (1u << 4) | (1u << 15) | ((uint32_t)(kMaxGroup >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 
 // MN-major operand with 128-byte swizzle: 64-element MN chunks of 128 B,
 // 8 K-rows per 1 KB atom; LBO = stride between MN chunks, SBO = stride
@@ -304,40 +299,62 @@ struct DecodeArgs {
   const float* out_scale;
   const float *k_global, *v_global;
   int* status;
-  int batch, table_width, page_size, kvheads, qheads, group, persistent;
+  int batch, table_width, page_size, page_shift, kvheads, qheads, group, persistent;
   float softmax_scale;
 };
 
-// One key's K and V bytes for the CTA's KV head (zeros past the length).
-struct KeyBytes {
-  uint4 k[4], v[4];
-  uint2 ks, vs;
+// The block's bytes one thread loads.  Loads are coalesced 256-bit vectors:
+// thread (warp w, lane l) reads the 32-byte half l % 2 of key rows
+// 32 w + 16 j + l / 2 (j = 0, 1), so one warp instruction covers 16 keys x 64
+// contiguous bytes (a key per thread would touch 32 lines per instruction and
+// load-issue would throttle).  Even lanes also read the key's K scales, odd
+// lanes its V scales (one instruction for both).
+struct BlockBytes {
+  uint4 k[2][2], v[2][2];  // [j][16-byte chunk of the 32-byte half]
+  uint2 s[2];
 };
+
+__device__ __forceinline__ int load_key_index(int warp, int lane, int j) { return warp * 32 + j * 16 + (lane >> 1); }
+
+__device__ __forceinline__ void ld256(const uint8_t* p, uint4& lo, uint4& hi) {
+  asm volatile("ld.global.cs.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(lo.x), "=r"(lo.y), "=r"(lo.z), "=r"(lo.w), "=r"(hi.x), "=r"(hi.y), "=r"(hi.z), "=r"(hi.w)
+               : "l"(p));
+}
+__device__ __forceinline__ uint2 ld64(const uint8_t* p) {
+  uint2 r;
+  asm volatile("ld.global.cs.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+  return r;
+}
 
 // Page id of a key (-1 past the length).  Looked up two blocks ahead of use,
 // so the dependent table load never stalls the key loads.
 __device__ __forceinline__ int page_of(const DecodeArgs& a, int r, int key, int length) {
-  return key < length ? __ldg(a.table + (int64_t)r * a.table_width + key / a.page_size) : -1;
+  return key < length ? __ldg(a.table + (int64_t)r * a.table_width + (key >> a.page_shift)) : -1;
+}
+__device__ __forceinline__ void block_pages(const DecodeArgs& a, int r, int base, int length, int warp, int lane,
+                                            int* pg) {
+#pragma unroll
+  for (int j = 0; j < 2; ++j) pg[j] = page_of(a, r, base + load_key_index(warp, lane, j), length);
 }
 
-__device__ __forceinline__ void load_key(const DecodeArgs& a, int h, int key, int page, KeyBytes& kb) {
-  if (page >= 0) {
-    const int entry = key % a.page_size;
-    const int64_t d = (int64_t)page * a.data_page + (int64_t)entry * a.data_row + (int64_t)h * a.data_head;
-    const int64_t s = (int64_t)page * a.sf_page + (int64_t)entry * a.sf_row + (int64_t)h * a.sf_head;
-    const uint4* kp = reinterpret_cast<const uint4*>(a.kc + d);
-    const uint4* vp = reinterpret_cast<const uint4*>(a.vc + d);
+__device__ __forceinline__ void load_block(const DecodeArgs& a, int h, int base, const int* pg, int warp, int lane,
+                                           BlockBytes& bb) {
+  const int hf = lane & 1;
+  const uint8_t* sbuf = hf ? a.vs : a.ks;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      kb.k[i] = __ldcs(kp + i);
-      kb.v[i] = __ldcs(vp + i);
+  for (int j = 0; j < 2; ++j) {
+    if (pg[j] >= 0) {
+      const int entry = (base + load_key_index(warp, lane, j)) & (a.page_size - 1);
+      const int64_t d = (int64_t)pg[j] * a.data_page + (int64_t)entry * a.data_row + (int64_t)h * a.data_head + hf * 32;
+      const int64_t s = (int64_t)pg[j] * a.sf_page + (int64_t)entry * a.sf_row + (int64_t)h * a.sf_head;
+      ld256(a.kc + d, bb.k[j][0], bb.k[j][1]);
+      ld256(a.vc + d, bb.v[j][0], bb.v[j][1]);
+      bb.s[j] = ld64(sbuf + s);
+    } else {
+      bb.k[j][0] = bb.k[j][1] = bb.v[j][0] = bb.v[j][1] = make_uint4(0, 0, 0, 0);
+      bb.s[j] = make_uint2(0, 0);
     }
-    kb.ks = __ldcs(reinterpret_cast<const uint2*>(a.ks + s));
-    kb.vs = __ldcs(reinterpret_cast<const uint2*>(a.vs + s));
-  } else {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) kb.k[i] = kb.v[i] = make_uint4(0, 0, 0, 0);
-    kb.ks = kb.vs = make_uint2(0, 0);
   }
 }
 
@@ -371,6 +388,8 @@ __device__ __forceinline__ void store_out(const DecodeArgs& a, int r, int qh, in
   }
 }
 
+// Three CTAs per SM (shared memory); a fourth, with 128 registers a thread,
+// measured slower.
 template <int GP>
 __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const DecodeArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -381,6 +400,7 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const DecodeArgs a)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_o + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* s_last = reinterpret_cast<int*>(tmem_slot + 2);
+  float* cg = reinterpret_cast<float*>(sm + kOffMisc + 32);  // [kQTerms] scale2 / g_t of the current task
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int h = blockIdx.x % a.kvheads, owner = blockIdx.x / a.kvheads;
@@ -428,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const DecodeArgs a)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-  const uint32_t sV = smem_u32(sm + kOffV), sQ = smem_u32(sm + kOffQ), sP = smem_u32(sm + kOffP);
+  const uint32_t sV = smem_u32(sm + kOffV), sK = smem_u32(sm + kOffK), sQ = sK + kQHalf, sP = smem_u32(sm + kOffP);
   const float scale2 = __fmul_rn(__fmul_rn(a.softmax_scale, *a.k_global), 1.4426950408889634f);
   const float vglob = *a.v_global;
   uint32_t phase_s = 0, phase_o = 0;
@@ -441,25 +461,77 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const DecodeArgs a)
     if (a.lengths[r] > cap && tid == 0 && h == 0 && slot == a.requests[r].first) report(a.status, QI_STATUS_BAD_LENGTH);
     const QiDecodeRange range = a.requests[r];
 
-    // Q^T operand: rows = the group's query heads (f16), rows >= G zero.
+    // The query group as a sum of kQTerms NVFP4 rows, the B operand of the S
+    // product: row n = 16 t + j holds term t of query head j (rows of heads
+    // >= G are zero).  Term t quantises the residual the earlier terms left,
+    // per 16 elements, with a power-of-two global scale
+    // g_t = 2^floor(log2(2688 / amax_t)) (amax over the whole group), so its
+    // values code * scale / g_t are exact in fp32 and each term removes about
+    // 3.5 bits of the residual: four leave ~1e-4 of the group's largest value.
+    // S = sum_t (K . term_t) / g_t, combined per head in registers
+    // (cg[t] = scale2 / g_t).  Thread <-> (head j = tid / 8, block b = tid % 8).
+    {
+      const int j = tid >> 3, b = tid & 7;
+      float rv[16];
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int row = tid >> 3, chunk = tid & 7, d0 = i * 64 + chunk * 8;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (row < G) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(a.q + ((int64_t)r * a.qheads + h * G + row) * kD + d0);
+      for (int i = 0; i < 2; ++i) {
+        uint4 raw = make_uint4(0, 0, 0, 0);
+        if (j < G) raw = *reinterpret_cast<const uint4*>(a.q + ((int64_t)r * a.qheads + h * G + j) * kD + b * 16 + i * 8);
         const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-        uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 f = __bfloat1622float2(b2[e]);
-          const __half2 hh = __floats2half2_rn(f.x, f.y);
-          w[e] = *reinterpret_cast<const uint32_t*>(&hh);
+          rv[i * 8 + 2 * e] = f.x;
+          rv[i * 8 + 2 * e + 1] = f.y;
         }
-        v = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      *reinterpret_cast<uint4*>(sm + kOffQ + i * 2048 + (row >> 3) * 1024 + (row & 7) * 128 +
-                                ((chunk ^ (row & 7)) * 16)) = v;
+      float* tred = red + 4 * kMaxGroup;  // [kQTerms][4 warps]
+#pragma unroll
+      for (int t = 0; t < kQTerms; ++t) {
+        float am = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) am = fmaxf(am, fabsf(rv[e]));
+        am = warp_max_butterfly(am);
+        if (lane == 0) tred[t * 4 + warp] = am;
+        __syncthreads();
+        const float amax = fmaxf(fmaxf(tred[t * 4], tred[t * 4 + 1]), fmaxf(tred[t * 4 + 2], tred[t * 4 + 3]));
+        uint2 packed = make_uint2(0, 0);
+        uint32_t sf = 0;
+        float ig = 0.0f;
+        if (amax > 0.0f) {  // CTA-uniform
+          const float y = fminf(fmaxf(__fdiv_rn(2688.0f, amax), 0x1p-100f), 0x1p100f);
+          const float g = __uint_as_float(__float_as_uint(y) & 0x7F800000u);  // 2^floor(log2 y)
+          ig = __uint_as_float((254u << 23) - __float_as_uint(g));            // 1 / g, exact
+          sf = nvfp4_quant16(rv, g, packed);
+          const float sc = e4m3_to_f(sf);
+          uint32_t hv[8];
+          e2m1x8_to_f16x8(packed.x, hv);
+          e2m1x8_to_f16x8(packed.y, hv + 4);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const uint32_t bits = (e & 1) ? hv[e >> 1] >> 16 : hv[e >> 1] & 0xFFFFu;
+            const float cv = __half2float(__ushort_as_half((unsigned short)bits));
+            rv[e] = __fsub_rn(rv[e], __fmul_rn(__fmul_rn(cv, sc), ig));
+          }
+        }
+        if (tid == 0) cg[t] = __fmul_rn(ig, scale2);
+        const int n = t * kMaxGroup + j;
+        *reinterpret_cast<uint2*>(sm + kOffK + (n >> 3) * 1024 + (n & 7) * 128 + (((4 + (b >> 1)) ^ (n & 7)) * 16) +
+                                  (b & 1) * 8) = packed;
+        sm[kOffSfq + n * 8 + b] = (uint8_t)sf;
+      }
+      __syncthreads();
+      // Term scales -> TMEM in the MMA's scale layout: lane l of every lane
+      // quarter, column 4 kk + c, holds the four scales (K block kk) of row
+      // l + 32 c; rows 64..127 do not exist (N = 64) and stay zero.
+      uint32_t v[8];
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          v[kk * 4 + c] = c < 2 ? *reinterpret_cast<const uint32_t*>(sm + kOffSfq + (lane + 32 * c) * 8 + kk * 4) : 0u;
+      __syncwarp();
+      tmem_st8w(tmem + lane_base + kColSfb, v);
     }
 
     float m_run[GP], l_thr[GP];
@@ -468,35 +540,40 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const DecodeArgs a)
     bool first_pv = true;
 
     // Blocks of the task: tiles begin, begin + stride, ... < end; two
-    // 128-key blocks per tile while inside the length.  Registers hold the
-    // current block's bytes (loaded during the previous block) and the page
-    // id of the next block (looked up one block earlier).
+    // 128-key blocks per tile while inside the length.  Block i's bytes are
+    // loaded into registers during block i - 1, issued right after block
+    // i - 1's S product (the load issue overlaps the MMA), and their page ids
+    // are looked up during block i - 2.
     int tile = task.begin, sub = 0;
     bool have = tile < task.end;
-    int t1 = tile, s1 = sub;  // the block after the current one
+    int t1 = tile, s1 = sub;  // the blocks 1 and 2 after the current one
     next_block(t1, s1, task.stride, L);
-    KeyBytes kb;
-    int page1 = -1;
+    int t2 = t1, s2 = s1;
+    next_block(t2, s2, task.stride, L);
+    BlockBytes bb;
+    int pg1[2] = {-1, -1};  // page ids of the block after the current one
     if (have) {
-      const int key0 = tile * kTile + tid;
-      load_key(a, h, key0, page_of(a, r, key0, L), kb);
-      if (t1 < task.end) page1 = page_of(a, r, t1 * kTile + s1 * kBlock + tid, L);
+      int pg0[2];
+      block_pages(a, r, tile * kTile, L, warp, lane, pg0);
+      load_block(a, h, tile * kTile, pg0, warp, lane, bb);
+      if (t1 < task.end) block_pages(a, r, t1 * kTile + s1 * kBlock, L, warp, lane, pg1);
     }
     while (have) {
       const int key = tile * kTile + sub * kBlock + tid;
       const bool valid = key < L;
       const bool have_next = t1 < task.end;
-      int t2 = t1, s2 = s1;  // two blocks ahead
-      next_block(t2, s2, task.stride, L);
 
-      // K row -> TMEM (lane = key).  tcgen05.st/ld/wait are .sync.aligned:
-      // the warp reconverges first after every divergent load or wait.
-      __syncwarp();
-      uint32_t pairs[32];
+      // K codes -> shared memory (A operand, row = key, 128-byte swizzle),
+      // K scales -> the exchange table.  The previous block's S product has
+      // finished with both (its barrier was waited on).
+      const int hf = lane & 1;
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        dequant_half(kb.k, kb.ks, half, pairs);
-        tmem_st32w(tmem + lane_base + kColK + half * 32, pairs);
+      for (int j = 0; j < 2; ++j) {
+        const int kr = load_key_index(warp, lane, j);
+        uint8_t* krow = sm + kOffK + (kr >> 3) * 1024 + (kr & 7) * 128;
+        *reinterpret_cast<uint4*>(krow + (((2 * hf) ^ (kr & 7)) * 16)) = bb.k[j][0];
+        *reinterpret_cast<uint4*>(krow + (((2 * hf + 1) ^ (kr & 7)) * 16)) = bb.k[j][1];
+        if (hf == 0) *reinterpret_cast<uint2*>(sm + kOffSfk + kr * 8) = bb.s[j];
       }
       // The previous PV product still reads V and P.
       if (!first_pv) {
@@ -505,19 +582,46 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const DecodeArgs a)
       }
       ok = __syncthreads_and(ok);
       if (!ok) break;
-      // V row -> shared memory, natural [key][D] order, 128-byte swizzle.
+      {  // K scales -> TMEM: lane l of each quarter, column 4 kk + c <- key l + 32 c
+        uint32_t v[8];
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        dequant_half(kb.v, kb.vs, half, pairs);
-        uint8_t* row = sm + kOffV + half * kVHalf + (tid >> 3) * 1024 + (tid & 7) * 128;
+        for (int kk = 0; kk < 2; ++kk)
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<uint4*>(row + ((c ^ (tid & 7)) * 16)) =
-              make_uint4(pairs[4 * c], pairs[4 * c + 1], pairs[4 * c + 2], pairs[4 * c + 3]);
+          for (int c = 0; c < 4; ++c)
+            v[kk * 4 + c] = *reinterpret_cast<const uint32_t*>(sm + kOffSfk + (lane + 32 * c) * 8 + kk * 4);
+        tmem_st8w(tmem + lane_base + kColSfa, v);
       }
-      if (have_next) {
-        load_key(a, h, t1 * kTile + s1 * kBlock + tid, page1, kb);
-        page1 = t2 < task.end ? page_of(a, r, t2 * kTile + s2 * kBlock + tid, L) : -1;
+      // V -> shared memory as f16, natural [key][D] order, 128-byte swizzle:
+      // a thread's 32 bytes of a key are the 64 elements of D-half hf (scale
+      // groups 4 hf .. 4 hf + 3: word hf of the V scales its odd partner lane
+      // loaded).
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int kr = load_key_index(warp, lane, j);
+        const uint32_t sx = __shfl_sync(0xffffffffu, bb.s[j].x, lane | 1);
+        const uint32_t sy = __shfl_sync(0xffffffffu, bb.s[j].y, lane | 1);
+        const uint32_t sw = hf ? sy : sx;
+        const uint32_t s01 = e4m3x2_to_f16x2(sw & 0xFFFFu), s23 = e4m3x2_to_f16x2(sw >> 16);
+        uint8_t* row = sm + kOffV + hf * kVHalf + (kr >> 3) * 1024 + (kr & 7) * 128;
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {  // 16-byte code chunk: 32 elements, groups 2 q, 2 q + 1
+          const uint4 cv = bb.v[j][q];
+          const uint32_t words[4] = {cv.x, cv.y, cv.z, cv.w};
+          uint32_t pairs[16];
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            const int group = 2 * q + (w >> 1);
+            const uint32_t s2 = splat_half(group < 2 ? s01 : s23, group & 1);
+            uint32_t f[4];
+            e2m1x8_to_f16x8(words[w], f);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) pairs[w * 4 + e] = hmul2u(f[e], s2);
+          }
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(row + (((4 * q + c) ^ (kr & 7)) * 16)) =
+                make_uint4(pairs[4 * c], pairs[4 * c + 1], pairs[4 * c + 2], pairs[4 * c + 3]);
+        }
       }
       __syncwarp();
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -527,18 +631,42 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const DecodeArgs a)
       if (tid == 0) {
         tc_fence_after();
 #pragma unroll
-        for (int s = 0; s < kD / 16; ++s)
-          mma_ts(tmem + kColS, tmem + kColK + s * 8, sdesc_kmajor_sw128(sQ + (s >> 2) * 2048 + (s & 3) * 32),
-                 kIdescS, s > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 2; ++kk)
+          mma_nvfp4(tmem + kColS, sdesc_kmajor_sw128(sK + kk * 32), sdesc_kmajor_sw128(sQ + kk * 32), kIdescS,
+                    tmem + kColSfa + kk * 4, tmem + kColSfb + kk * 4, (uint32_t)kk);
         tc_commit(bar_s);
+      }
+      // The next block's loads, issued while the S product runs.
+      if (have_next) {
+        load_block(a, h, t1 * kTile + s1 * kBlock, pg1, warp, lane, bb);
+        if (t2 < task.end) block_pages(a, r, t2 * kTile + s2 * kBlock, L, warp, lane, pg1);
+        else pg1[0] = pg1[1] = -1;
       }
       __syncwarp();
       ok = mbar_wait(bar_s, phase_s, abort_flag, a.status);
       phase_s ^= 1;
       __syncwarp();
       tc_fence_after();
+      // S per head: the four term columns, each times scale2 / g_t.
+      // (GP = 16 reads one term per round trip to stay within the registers.)
+      constexpr int kTermsPerLoad = GP == 16 ? 1 : 2;
       float sv[16];
-      tmem_ld16(tmem + lane_base + kColS, sv);
+#pragma unroll
+      for (int t0 = 0; t0 < kQTerms; t0 += kTermsPerLoad) {
+        uint32_t d[kTermsPerLoad][GP];
+#pragma unroll
+        for (int u = 0; u < kTermsPerLoad; ++u) {
+          if constexpr (GP == 16) tmem_ld16_async(tmem + lane_base + kColS + (t0 + u) * kMaxGroup, d[u]);
+          else tmem_ld8_async(tmem + lane_base + kColS + (t0 + u) * kMaxGroup, d[u]);
+        }
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int j = 0; j < GP; ++j)
+#pragma unroll
+          for (int u = 0; u < kTermsPerLoad; ++u)
+            sv[j] = t0 + u == 0 ? __fmul_rn(__uint_as_float(d[0][j]), cg[0])
+                                : __fmaf_rn(__uint_as_float(d[u][j]), cg[t0 + u], sv[j]);
+      }
       // Deferred maximum: the running maxima m stay while no score of the
       // block exceeds them by more than 8 (P <= 2^8, exact enough in f16);
       // otherwise (and on a task's first block) all heads move to the block
@@ -546,7 +674,7 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const DecodeArgs a)
       bool grow = first_pv;
 #pragma unroll
       for (int j = 0; j < GP; ++j) {
-        sv[j] = valid ? __fmul_rn(sv[j], scale2) : -INFINITY;
+        sv[j] = valid ? sv[j] : -INFINITY;
         grow |= sv[j] > m_run[j] + kMaxLag;
       }
       if (__syncthreads_or(grow || !ok)) {
@@ -601,6 +729,7 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const DecodeArgs a)
       first_pv = false;
       tile = t1, sub = s1, have = have_next;
       t1 = t2, s1 = s2;
+      next_block(t2, s2, task.stride, L);
     }
     if (!ok) break;
     if (!first_pv) {
@@ -684,6 +813,28 @@ static cudaError_t configure(Kernel kernel) {
   return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
 }
 
+// Resident CTAs per SM of one kernel from its own limits: registers
+// (256-register warp granules), shared memory (plus the 1 KB the system
+// reserves per CTA) and tensor memory (512 columns).  (The runtime occupancy
+// query does not know the tensor-memory limit.)
+template <class Kernel>
+static int resident_ctas(Kernel kernel, int* regs, int* local) {
+  cudaError_t e = configure(kernel);
+  if (e != cudaSuccess) return -(int)e;
+  cudaFuncAttributes attr;
+  e = cudaFuncGetAttributes(&attr, kernel);
+  if (e != cudaSuccess) return -(int)e;
+  int dev = 0, smem_sm = 0, regs_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+  cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev);
+  const int warp_regs = (attr.numRegs * 32 + 255) / 256 * 256;
+  *regs = attr.numRegs;
+  *local = (int)attr.localSizeBytes;
+  return std::min(std::min(regs_sm / (warp_regs * (kThreads / 32)), smem_sm / ((int)kSmemBytes + 1024)),
+                  512 / (int)kTmemCols);
+}
+
 extern "C" {
 
 static int decode_check(const QiDecode* p) {
@@ -691,7 +842,9 @@ static int decode_check(const QiDecode* p) {
       p->table_width < 1 || p->mode < 0 || p->mode > 2 || (p->persistent && p->mode != 0))
     return (int)cudaErrorInvalidValue;
   const QiKvView& kv = p->kv;
-  if (kv.head_dim != kD || kv.kvheads < 1 || kv.page_size < 1 || p->qheads < kv.kvheads ||
+  // Pages of a power-of-two token count (the page of a key is a shift).
+  if (kv.head_dim != kD || kv.kvheads < 1 || kv.page_size < 1 || (kv.page_size & (kv.page_size - 1)) ||
+      p->qheads < kv.kvheads ||
       p->qheads % kv.kvheads || p->qheads / kv.kvheads > kMaxGroup ||
       (int64_t)p->table_width * kv.page_size > (int64_t)0x7fffffff - (kTile - 1))
     return (int)cudaErrorInvalidValue;
@@ -713,10 +866,11 @@ int qi_decode_attention(const QiDecode* p, cudaStream_t stream) {
   if (!p->q || !kv.k_cache || !kv.v_cache || !kv.k_scales || !kv.v_scales || !p->block_table || !p->semaphores ||
       !p->scratch || !p->out || !p->k_global || !p->v_global || (p->gate && !p->out_scale))
     return (int)cudaErrorInvalidValue;
-  // 16-byte code loads, 8-byte scale loads, 16-byte Q loads.
+  // 32-byte code loads, 8-byte scale loads, 16-byte Q loads.
+  auto a32 = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 31) == 0; };
   auto a16 = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) == 0; };
   auto a8 = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 7) == 0; };
-  if (!a16(kv.k_cache) || !a16(kv.v_cache) || kv.data_page % 16 || kv.data_row % 16 || kv.data_head % 16 ||
+  if (!a32(kv.k_cache) || !a32(kv.v_cache) || kv.data_page % 32 || kv.data_row % 32 || kv.data_head % 32 ||
       !a8(kv.k_scales) || !a8(kv.v_scales) || kv.sf_page % 8 || kv.sf_row % 8 || kv.sf_head % 8 || !a16(p->q) ||
       !a16(p->scratch) || (reinterpret_cast<uintptr_t>(p->out) & 1) || (reinterpret_cast<uintptr_t>(p->gate) & 1))
     return (int)cudaErrorInvalidValue;
@@ -746,6 +900,8 @@ int qi_decode_attention(const QiDecode* p, cudaStream_t stream) {
   a.v_global = p->v_global;
   a.status = p->status;
   a.batch = p->batch, a.table_width = p->table_width, a.page_size = kv.page_size;
+  a.page_shift = 0;
+  while ((1 << a.page_shift) < kv.page_size) ++a.page_shift;
   a.kvheads = kv.kvheads, a.qheads = p->qheads, a.group = p->qheads / kv.kvheads;
   a.persistent = p->persistent;
   a.softmax_scale = p->softmax_scale;
@@ -769,30 +925,21 @@ int qi_decode_attention(const QiDecode* p, cudaStream_t stream) {
 
 int qi_decode_resources(int* values) {
   if (!values) return (int)cudaErrorInvalidValue;
-  cudaError_t e = configure(decode_kernel<8>);
-  if (e != cudaSuccess) return (int)e;
-  cudaFuncAttributes attr;
-  e = cudaFuncGetAttributes(&attr, decode_kernel<8>);
-  if (e != cudaSuccess) return (int)e;
-  // Resident CTAs per SM from the kernel's own limits: registers (256-register
-  // warp granules), shared memory (plus the 1 KB the system reserves per CTA)
-  // and tensor memory (512 columns).  (The runtime occupancy query does not
-  // know the tensor-memory limit, and on this kernel reports 1 where 3 run.)
-  int dev = 0, smem_sm = 0, regs_sm = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
-  cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev);
-  const int warp_regs = (attr.numRegs * 32 + 255) / 256 * 256;
-  const int resident = std::min(std::min(regs_sm / (warp_regs * (kThreads / 32)), smem_sm / ((int)kSmemBytes + 1024)),
-                                512 / (int)kTmemCols);
+  int regs8 = 0, local8 = 0, regs16 = 0, local16 = 0;
+  const int r8 = resident_ctas(decode_kernel<8>, &regs8, &local8);
+  if (r8 < 0) return -r8;
+  const int r16 = resident_ctas(decode_kernel<16>, &regs16, &local16);
+  if (r16 < 0) return -r16;
   values[0] = (int)sizeof(QiDecode);
-  values[1] = attr.numRegs;
+  values[1] = regs8;
   values[2] = (int)kSmemBytes;
-  values[3] = (int)attr.localSizeBytes;
-  values[4] = resident;
+  values[3] = std::max(local8, local16);
+  values[4] = r8;
   values[5] = (int)sizeof(QiDecodeTask);
   values[6] = (int)sizeof(QiDecodeRange);
   values[7] = (int)sizeof(QiDecodeBucket);
+  values[8] = regs16;
+  values[9] = r16;
   return 0;
 }
 

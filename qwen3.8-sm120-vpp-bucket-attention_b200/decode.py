@@ -61,19 +61,22 @@ def route(lengths, *, table_width, sm_count, forced="auto", page_size=16, diagno
                 reason="geometry")
 
 
-def resources():
-    """Kernel resources: registers, shared bytes, local bytes, resident CTAs per SM."""
-    vals = (ct.c_int * 8)()
+def resources(group=8):
+    """Kernel resources for groups of ``group`` query heads per KV head:
+    registers, shared bytes, local bytes, resident CTAs per SM."""
+    vals = (ct.c_int * 10)()
     N.check(N.lib().qi_decode_resources(vals), "qi_decode_resources")
     if (vals[0], vals[5], vals[6], vals[7]) != (ct.sizeof(N.QiDecode), 16, 8, 8):
         raise RuntimeError("decode C / Python ABI mismatch")
-    return dict(registers=vals[1], shared_bytes=vals[2], local_bytes=vals[3], resident_ctas=vals[4], threads=128)
+    small = group <= 8
+    return dict(registers=vals[1] if small else vals[8], shared_bytes=vals[2], local_bytes=vals[3],
+                resident_ctas=vals[4] if small else vals[9], threads=128)
 
 
-def default_ctas(batch, kvheads, device=None):
+def default_ctas(batch, kvheads, device=None, group=8):
     """Task slots that fill the GPU once: SMs x resident CTAs per SM / Hkv."""
     sms = torch.cuda.get_device_properties(device).multi_processor_count
-    return max(batch, min(MAX_CTAS, sms * resources()["resident_ctas"] // kvheads))
+    return max(batch, min(MAX_CTAS, sms * resources(group)["resident_ctas"] // kvheads))
 
 
 def _check_batch(batch, ctas):
@@ -158,12 +161,12 @@ class Workspace:
 
     def __init__(self, batch, *, qheads, kvheads, ctas=None, page_size=16, device="cuda", plan=None):
         device = torch.device(device)
-        if ctas is None:
-            ctas = default_ctas(batch, kvheads, device)
-        _check_batch(batch, ctas)
         if type(qheads) is not int or type(kvheads) is not int or kvheads < 1 or qheads % kvheads \
                 or qheads // kvheads > 16:
             raise ValueError("expected qheads = G * kvheads with G <= 16")
+        if ctas is None:
+            ctas = default_ctas(batch, kvheads, device, group=qheads // kvheads)
+        _check_batch(batch, ctas)
         self.batch, self.ctas, self.qheads, self.kvheads = batch, ctas, qheads, kvheads
         self.plan = plan if plan is not None else TaskPlan(batch, ctas=ctas, page_size=page_size, device=device)
         if self.plan.batch != batch or self.plan.ctas != ctas or self.plan.tasks.device != device:

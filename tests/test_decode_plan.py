@@ -87,3 +87,25 @@ def test_blockwise_oracle_against_exact_softmax():
                                          v_global=2.0)
         assert np.abs(got - want).max() <= 2e-3 * np.abs(want).max()
         assert not got[0].any()
+
+
+@pytest.mark.parametrize("scale", [1e-3, 1.0, 300.0])
+def test_query_terms_reconstruct_the_group(scale):
+    """The S product's NVFP4 query terms: power-of-two globals, exact term
+    values, and a residual that shrinks about 11x per term."""
+    from oracle import formats as F
+    q = F.bf16_round(np.random.default_rng(3).standard_normal((12, 128)).astype(np.float32) * np.float32(scale))
+    q[5] = 0.0  # a zero head contributes nothing
+    terms = OD.q_terms(q)
+    assert len(terms) == OD.Q_TERMS
+    approx = np.zeros_like(q, dtype=np.float64)
+    errs = []
+    for unscaled, ig in terms:
+        assert ig > 0 and math.frexp(ig)[0] == 0.5  # 1/g is a power of two
+        assert not unscaled[5].any()
+        approx += unscaled.astype(np.float64) * ig
+        errs.append(np.abs(approx - q).max() / np.abs(q).max())
+    assert all(b < a / 5 for a, b in zip(errs, errs[1:])), errs
+    assert errs[-1] < 2e-4
+    zero = OD.q_terms(np.zeros((4, 128), np.float32))
+    assert all(ig == 0.0 and not t.any() for t, ig in zero)
