@@ -18,8 +18,10 @@
 //     rejected with cudaErrorInvalidValue before anything is launched;
 //   * all calls share the one array, so calls whose work overlaps on the GPU
 //     (different streams without ordering between them) race on it; order
-//     them on one stream.  Nothing in it has to start at zero: every byte the
-//     attention reads is written by the dequantisation of the same call.
+//     them on one stream.  Nothing in the scratch array has to start at zero:
+//     every byte the attention reads is written by the dequantisation of the
+//     same call.  The split workspace's arrival counters must start even;
+//     every call clears them first (cudaMemsetAsync, which allocates nothing).
 //   * the first call on a device looks the array's device address up (with
 //     that device current) and caches it; make that first call before any
 //     stream capture.
@@ -89,6 +91,8 @@ extern "C" int qi_paged_prefill_attention_noalloc(const QiKvView* kv, const int3
   e = scratch_address(device, &scratch, &split);
   if (e != cudaSuccess) return (int)e;
   unsigned char* base = static_cast<unsigned char*>(scratch);
+  e = cudaMemsetAsync(split, 0, 4096, stream);  // arrival counters of the split units
+  if (e != cudaSuccess) return (int)e;
   int rc = qi_kv_dequant(kv, block_table, (int)tokens, base, base + k_span, vt_row, stream);
   if (rc) return rc;
   QiAttention a{};
