@@ -63,6 +63,8 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-kernel-timing", action="store_true")
     p.add_argument("--layers", type=int, default=None, help="override layer count (must split into 2N stages)")
+    p.add_argument("--overlap", choices=("auto", "on", "off"), default="auto",
+                   help="one GPU: run the two virtual stages on two CUDA streams (auto: on for N=1)")
     p.add_argument("--kv-shadow", choices=("auto", "on", "off"), default="auto",
                    help="keep each request's f16 K/V^T across its chunks (dequantise new tokens only)")
     p.add_argument("--workload", choices=("prefill", "decode"), default="prefill",
@@ -247,7 +249,8 @@ def run_ours(args):
                                     profile=args.profile)
     request_tokens = [args.prompt_tokens] * args.requests
     runner = FoldedRank(shape, rank, world, dev, request_tokens, args.chunk_size, transport=transport,
-                        profile=args.profile, kv_shadow={"auto": None, "on": True, "off": False}[args.kv_shadow])
+                        profile=args.profile, kv_shadow={"auto": None, "on": True, "off": False}[args.kv_shadow],
+                        overlap={"auto": None, "on": True, "off": False}[args.overlap])
     gen = torch.Generator(device=dev).manual_seed(4321)
     embeds = [torch.randn(t, shape.hidden, generator=gen, device=dev).to(torch.bfloat16) for t in request_tokens] \
         if rank == 0 else None
@@ -400,6 +403,7 @@ def run_ours(args):
                     prompt_tokens=args.prompt_tokens, chunk=args.chunk_size,
                     virtual_stages=2 * world if args.profile == "vpp" else world,
                     parallelism=f"folded-vpp pp{world}" if args.profile == "vpp" else f"pp{world}", transport=(args.transport if world > 1 else "local fold"),
+                    stage_streams=2 if runner.overlap else 1,
                     l2="inputs larger than L2 (weights ~16 GB, KV pages)"),
         bubble_fraction=bubble, busiest_rank_compute_ms=busiest, instrumented_bank_ms=makespan,
         model_tflops=total_flops / (ms / 1e3) / 1e12,

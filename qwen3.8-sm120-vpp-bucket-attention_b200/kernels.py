@@ -351,6 +351,18 @@ def attention_workspace(device, head_dim):
     return ws
 
 
+def attention_workspace_new(device, head_dim):
+    """A fresh zero-filled key-range split workspace (not the cached one): for
+    attention calls on a stream that may run concurrently with another."""
+    device = torch.device(device)
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    nbytes = ct.c_int64(0)
+    with torch.cuda.device(idx):
+        N.check(N.lib().qi_prefill_attention_workspace_bytes(head_dim, ct.byref(nbytes)),
+                "qi_prefill_attention_workspace_bytes")
+    return torch.zeros(nbytes.value, dtype=torch.uint8, device=torch.device("cuda", idx))
+
+
 def prefill_attention(q, k, vt, *, history, qheads, kvheads, head_dim, k_global, v_global, out=None,
                       softmax_scale=None, status=None, kv_tokens=None, workspace=None):
     """Causal GQA attention of ``rows`` queries at positions history.. over

@@ -171,6 +171,9 @@ class Workspace:
         self.vt = torch.empty(s.kvheads * d * vt_row, dtype=torch.float16, **e)
         self.status = torch.zeros(1, dtype=torch.int32, **e)
         self.ping = [torch.empty((max_rows, h), dtype=torch.bfloat16, **e) for _ in range(4)]
+        # The attention's key-range split workspace: one per workspace, so
+        # stages that run concurrently on two streams do not share it.
+        self.attn_ws = K.attention_workspace_new(device, d)
 
     def kv_views(self, shape, tokens):
         vt_row = (tokens + 63) // 64 * 64
@@ -184,7 +187,7 @@ class StageModel:
     for every request of a bank, and the stage forward."""
 
     def __init__(self, shape, layers, device, *, max_rows, request_tokens, base_seed=1234, on_device_init=None,
-                 final_norm=False, kv_shadow=None):
+                 final_norm=False, kv_shadow=None, streams=1):
         self.shape = shape
         self.device = torch.device(device)
         self.layers = list(layers)
@@ -200,7 +203,10 @@ class StageModel:
         self.kv = {l: K.PagedKV(int(offsets[-1]), s.page_size, s.kvheads, s.head_dim, self.device)
                    for l in self.layers}
         self.rope = rope_table(self.max_tokens, s.head_dim, s.rope_theta, self.device)
-        self.ws = Workspace(s, max_rows, self.max_tokens, self.device)
+        # One workspace per concurrently running stage (streams=2: the two
+        # virtual stages of a rank overlap on two CUDA streams).
+        self.ws_sets = [Workspace(s, max_rows, self.max_tokens, self.device) for _ in range(streams)]
+        self.ws = self.ws_sets[0]
         f = lambda v: torch.tensor([v], dtype=torch.float32, device=self.device)
         self.g_norm, self.g_down = f(ACT_GLOBAL_NORM), f(ACT_GLOBAL_DOWN)
         self.kg, self.vg = f(KV_GLOBAL_K), f(KV_GLOBAL_V)
@@ -238,8 +244,9 @@ class StageModel:
         slots = bt[(pos // s.page_size).long()] * s.page_size + pos % s.page_size
         return ChunkContext(request, history, rows, pos, slots.to(torch.int32), bt)
 
-    def layer_forward(self, layer, hidden, residual, ctx, hidden_out, residual_out, on_residual=None):
-        s, ws, w = self.shape, self.ws, self.weights[layer]
+    def layer_forward(self, layer, hidden, residual, ctx, hidden_out, residual_out, on_residual=None, ws=None):
+        s, w = self.shape, self.weights[layer]
+        ws = ws or self.ws
         rows = ctx.rows
         h, d = s.hidden, s.head_dim
         q_in, sf_in, res1 = K.norm_pack(hidden, residual, w.ln_in, self.g_norm, eps=s.eps, q=ws.q_in[:rows],
@@ -261,7 +268,7 @@ class StageModel:
             K.kv_dequant(kv, ctx.block_table, tokens, k_out=kd, vt_out=vt)
         att = K.prefill_attention(q, kd, vt, history=ctx.history, qheads=s.qheads, kvheads=s.kvheads, head_dim=d,
                                   k_global=self.kg, v_global=self.vg, out=ws.att[:rows],
-                                  softmax_scale=self.softmax_scale, status=ws.status)
+                                  softmax_scale=self.softmax_scale, status=ws.status, workspace=ws.attn_ws)
         if self.kv_shadow and tokens >= self.request_tokens[ctx.request]:
             del self.shadow[(ctx.request, layer)]  # last chunk: stream order keeps the buffers until read
         a8, s8 = K.gate_fp8(att, qkv[:, d:], fp8=ws.a8[:rows], scale=ws.s8[:rows], head_dim=d, head_stride=2 * d)
@@ -278,12 +285,15 @@ class StageModel:
                      out=hidden_out)
         return hidden_out, residual_out
 
-    def run_layers(self, span, hidden, residual, ctx, out_planes=None, on_residual=None):
+    def run_layers(self, span, hidden, residual, ctx, out_planes=None, on_residual=None, ws=None):
         """Run layers [lo, hi) on one chunk.  ``out_planes`` = (hidden, residual)
-        buffers that receive the final layer's output (e.g. a transport slot)."""
+        buffers that receive the final layer's output (e.g. a transport slot).
+        ``ws``: the workspace set (default the first); stages that run
+        concurrently need different ones."""
         lo, hi = span
         rows = ctx.rows
-        ping = [t[:rows] for t in self.ws.ping]
+        ws = ws or self.ws
+        ping = [t[:rows] for t in ws.ping]
         for i, layer in enumerate(range(lo, hi)):
             last = layer == hi - 1
             if last and out_planes is not None:
@@ -291,7 +301,7 @@ class StageModel:
             else:
                 ho, ro = ping[2 * (i % 2)], ping[2 * (i % 2) + 1]
             hidden, residual = self.layer_forward(layer, hidden, residual, ctx, ho, ro,
-                                                  on_residual if last else None)
+                                                  on_residual if last else None, ws)
         return hidden, residual
 
     def final_norm(self, hidden, residual, out=None):
@@ -309,6 +319,7 @@ class StageModel:
         return tokens
 
     def check_status(self):
-        st = int(self.ws.status.item())
-        if st:
-            raise RuntimeError(f"kernel status word {st:#x}")
+        for ws in self.ws_sets:
+            st = int(ws.status.item())
+            if st:
+                raise RuntimeError(f"kernel status word {st:#x}")

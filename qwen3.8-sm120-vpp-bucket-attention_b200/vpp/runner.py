@@ -47,7 +47,7 @@ class FoldedRank:
     stage rank of G, output on rank G-1."""
 
     def __init__(self, shape, rank, ranks, device, request_tokens, chunk, *, transport=None, base_seed=1234,
-                 on_device_init=None, keep_all_outputs=False, profile="vpp", kv_shadow=None):
+                 on_device_init=None, keep_all_outputs=False, profile="vpp", kv_shadow=None, overlap=None):
         if profile not in L.PROFILES:
             raise ValueError("profile is vpp or cpp")
         self.shape, self.rank, self.ranks, self.profile = shape, rank, ranks, profile
@@ -65,14 +65,28 @@ class FoldedRank:
             self.stage_count, self.output_rank = ranks, ranks - 1
             self.order = L.cpp_stage_orders(batches, ranks)[rank]
         layers = [layer for span in self.spans for layer in range(*span)]
+        # On one GPU the two virtual stages are both local: stage 0 of chunk
+        # j + 1 and stage 1 of chunk j are independent, so they run on two
+        # CUDA streams and each one's kernels fill the SMs the other leaves
+        # idle (partial last waves, small producers).  Default: on for the
+        # one-rank fold.
+        if overlap is None:
+            overlap = profile == "vpp" and ranks == 1 and self.device.type == "cuda"
+        self.overlap = bool(overlap) and profile == "vpp" and ranks == 1
         self.model = StageModel(shape, layers, self.device, max_rows=chunk, request_tokens=self.request_tokens,
                                 base_seed=base_seed, on_device_init=on_device_init,
-                                final_norm=(rank == self.output_rank), kv_shadow=kv_shadow)
+                                final_norm=(rank == self.output_rank), kv_shadow=kv_shadow,
+                                streams=2 if self.overlap else 1)
         self.transport = transport
         self.keep_all_outputs = keep_all_outputs
         h = shape.hidden
         self.fold = (torch.empty((chunk, h), dtype=torch.bfloat16, device=self.device),
                      torch.empty((chunk, h), dtype=torch.bfloat16, device=self.device))
+        # Overlapped fold: three (hidden, residual) pairs, chunk j in pair j % 3;
+        # stage 0 of chunk j waits for stage 1 of chunk j - 3 (the pair's last reader).
+        self.folds = [self.fold] + [(torch.empty_like(self.fold[0]), torch.empty_like(self.fold[1]))
+                                    for _ in range(2 if self.overlap else 0)]
+        self.streams = [torch.cuda.Stream(self.device) for _ in range(2)] if self.overlap else None
         self.last_hidden = torch.empty((len(self.request_tokens), h), dtype=torch.bfloat16, device=self.device)
         self.last_tokens = torch.full((len(self.request_tokens),), -1, dtype=torch.int32, device=self.device)
         self.outputs = {}
@@ -89,7 +103,10 @@ class FoldedRank:
         per request (list), or None with ``host_embeds`` (pinned host tensors,
         copied chunk by chunk inside the run).  On the output rank, returns the
         final-normed last hidden row of each request and leaves each request's
-        greedy output token in ``last_tokens``."""
+        greedy output token in ``last_tokens``.  ``record_events`` (per-stage
+        device times) runs the stages in series on the current stream."""
+        if self.overlap and not record_events:
+            return self._run_bank_overlapped(embeds, host_embeds)
         G = self.ranks
         last_stage = self.stage_count - 1
         folded = self.profile == "vpp"
@@ -141,6 +158,53 @@ class FoldedRank:
         if self.rank == self.output_rank:
             # P+1: the one output token of every request (greedy), part of the bank.
             self.model.sample(self.last_hidden, tokens=self.last_tokens)
+        return self.last_hidden
+
+    def _run_bank_overlapped(self, embeds, host_embeds):
+        """One-rank fold with stage 0 on one stream and stage 1 on another.
+        Order constraints: a stage's chunks run in order on its stream (the KV
+        history of chunk j + 1 is written by chunk j); stage 1 of chunk j waits
+        for stage 0 of chunk j (the fold pair); stage 0 of chunk j waits for
+        stage 1 of chunk j - 3 (the last reader of the pair it overwrites).
+        The caller's stream waits for both at the end."""
+        ctxs = self._contexts()
+        main = torch.cuda.current_stream(self.device)
+        start = torch.cuda.Event()
+        start.record(main)
+        for st in self.streams:
+            st.wait_event(start)
+        done = {}
+        for batch, stage in self.order:
+            ch, ctx = self.chunks[batch], ctxs[batch]
+            st = self.streams[stage]
+            fh, fr = self.folds[batch % 3]
+            with torch.cuda.stream(st):
+                if stage == 0:
+                    if batch >= 3:  # a KeyError here would mean an order that breaks the fold rotation
+                        st.wait_event(done[(batch - 3, 1)])
+                    if host_embeds is not None:
+                        hidden = host_embeds[ch.request][ch.start:ch.start + ch.rows].to(self.device,
+                                                                                           non_blocking=True)
+                    else:
+                        hidden = embeds[ch.request][ch.start:ch.start + ch.rows]
+                    self.model.run_layers(L.stage_layers(0, 1, self.shape.layers), hidden, None, ctx,
+                                          (fh[:ch.rows], fr[:ch.rows]), None, self.model.ws_sets[0])
+                else:
+                    st.wait_event(done[(batch, 0)])
+                    h, r = self.model.run_layers(L.stage_layers(1, 1, self.shape.layers), fh[:ch.rows],
+                                                 fr[:ch.rows], ctx, None, None, self.model.ws_sets[1])
+                    if self.keep_all_outputs:
+                        self.outputs[batch] = self.model.final_norm(h, r)
+                    if ch.start + ch.rows == self.request_tokens[ch.request]:
+                        self.model.final_norm(h[-1:], r[-1:], out=self.last_hidden[ch.request:ch.request + 1])
+                ev = torch.cuda.Event()
+                ev.record(st)
+                done[(batch, stage)] = ev
+        with torch.cuda.stream(self.streams[1]):
+            # P+1: the one output token of every request (greedy), part of the bank.
+            self.model.sample(self.last_hidden, tokens=self.last_tokens)
+        for st in self.streams:
+            main.wait_stream(st)
         return self.last_hidden
 
     def compute_ms(self):

@@ -196,6 +196,26 @@ def test_gate_fp8_reads_gate_in_place_from_qkv_rows(K):
     assert np.array_equal(fp8.cpu().numpy(), co)
 
 
+def test_gate_fp8_bit_exact_across_magnitudes(K):
+    """Rows whose values span the bf16 range (tiny, huge, a single outlier,
+    subnormal-sized), with a saturated gate so the FP8 quotients run over
+    the divisor range."""
+    rows, cols = 64, 8192
+    g = torch.Generator().manual_seed(35)
+    out = torch.randn(rows, cols, generator=g)
+    mags = torch.logspace(-36, 36, rows, base=2.0)
+    out = (out * mags[:, None]).to(torch.bfloat16)
+    out[7, 100] = 3.0e38  # one outlier sets the row's scale
+    out[9, :] = 1e-39  # subnormal-sized row
+    gate = torch.full((rows, cols), 20.0, dtype=torch.bfloat16)
+    gate[::2] = _bf16((rows // 2, cols), 36, 4.0)
+    fp8, scale = K.gate_fp8(out.to(DEV), gate.to(DEV))
+    co, so = P.gate_fp8(out.float().numpy(), gate.float().numpy())
+    torch.cuda.synchronize()
+    assert np.array_equal(scale.cpu().numpy(), so)
+    assert np.array_equal(fp8.cpu().numpy(), co)
+
+
 def test_weight_quantizers_bit_exact(K):
     w = torch.randn(512, 1024, generator=torch.Generator().manual_seed(41)) * 0.02
     qo, sfo, go = P.quantize_weight_nvfp4(w.numpy())

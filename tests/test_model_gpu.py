@@ -127,6 +127,36 @@ def test_bank_output_tokens_are_the_greedy_samples_of_its_final_hidden():
     assert all(0 <= t < M.TINY.vocab for t in got)
 
 
+def test_overlapped_stages_equal_the_serial_bank():
+    """One GPU: the two virtual stages on two streams (stage 0 of chunk j + 1
+    beside stage 1 of chunk j) give the bank of the stages run in series, bit
+    for bit (same kernels on the same values), over several banks in a row
+    (fold pairs and per-stage workspaces reused), with host-copied inputs too."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from qwen_infra_b200.vpp import model as M
+    from qwen_infra_b200.vpp.runner import FoldedRank
+
+    dev = torch.device("cuda:0")
+    tokens = [700, 512, 300, 900]
+    g = torch.Generator().manual_seed(9)
+    embeds = [torch.randn(t, M.TINY.hidden, generator=g).to(torch.bfloat16).to(dev) for t in tokens]
+    serial = FoldedRank(M.TINY, 0, 1, dev, tokens, 128, overlap=False, keep_all_outputs=True)
+    overlapped = FoldedRank(M.TINY, 0, 1, dev, tokens, 128, overlap=True, keep_all_outputs=True)
+    assert overlapped.overlap and not serial.overlap
+    want = serial.run_bank(embeds).clone()
+    want_tokens = serial.last_tokens.clone()
+    host = [e.cpu().pin_memory() for e in embeds]
+    for i in range(3):
+        got = overlapped.run_bank(None, host_embeds=host) if i == 2 else overlapped.run_bank(embeds)
+        torch.cuda.synchronize()
+        overlapped.model.check_status()
+        assert torch.equal(got, want)
+        assert torch.equal(overlapped.last_tokens, want_tokens)
+        for b, out in serial.outputs.items():
+            assert torch.equal(overlapped.outputs[b], out), b
+
+
 def test_27b_shape_layer_every_stage_and_end_to_end():
     """One 27B-shaped decoder layer (H5120, 64/8 heads, D128, I17408, page 16)
     on two 2048-row chunks of one request (history 0 and 2048), teacher-forced
