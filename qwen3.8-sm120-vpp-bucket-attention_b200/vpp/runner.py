@@ -65,14 +65,17 @@ class FoldedRank:
             self.stage_count, self.output_rank = ranks, ranks - 1
             self.order = L.cpp_stage_orders(batches, ranks)[rank]
         layers = [layer for span in self.spans for layer in range(*span)]
-        # On one GPU the two virtual stages are both local: stage 0 of chunk
-        # j + 1 and stage 1 of chunk j are independent, so they run on two
+        # A folded rank owns two virtual stages whose chunks are independent
+        # of each other at any moment (the first traversal's stage on chunk
+        # j + k beside the second traversal's on chunk j), so they run on two
         # CUDA streams and each one's kernels fill the SMs the other leaves
-        # idle (partial last waves, small producers).  Default: on for the
-        # one-rank fold.
-        if overlap is None:
-            overlap = profile == "vpp" and ranks == 1 and self.device.type == "cuda"
-        self.overlap = bool(overlap) and profile == "vpp" and ranks == 1
+        # idle (partial last waves, small producers).  Default: on for the fold
+        # on one GPU or over the peer-to-peer transport (whose boundary waits
+        # are events on the consuming stream); the NCCL comparison transport
+        # keeps the single stream.
+        p2p = transport is not None and getattr(transport, "backend", None) == "p2p"
+        can = profile == "vpp" and (ranks == 1 or p2p) and self.device.type == "cuda"
+        self.overlap = can if overlap is None else (bool(overlap) and can)
         self.model = StageModel(shape, layers, self.device, max_rows=chunk, request_tokens=self.request_tokens,
                                 base_seed=base_seed, on_device_init=on_device_init,
                                 final_norm=(rank == self.output_rank), kv_shadow=kv_shadow,
@@ -83,7 +86,8 @@ class FoldedRank:
         self.fold = (torch.empty((chunk, h), dtype=torch.bfloat16, device=self.device),
                      torch.empty((chunk, h), dtype=torch.bfloat16, device=self.device))
         # Overlapped fold: three (hidden, residual) pairs, chunk j in pair j % 3;
-        # stage 0 of chunk j waits for stage 1 of chunk j - 3 (the pair's last reader).
+        # stage G-1 of chunk j waits for stage G of chunk j - 3 (the pair's
+        # last reader).
         self.folds = [self.fold] + [(torch.empty_like(self.fold[0]), torch.empty_like(self.fold[1]))
                                     for _ in range(2 if self.overlap else 0)]
         self.streams = [torch.cuda.Stream(self.device) for _ in range(2)] if self.overlap else None
@@ -161,38 +165,63 @@ class FoldedRank:
         return self.last_hidden
 
     def _run_bank_overlapped(self, embeds, host_embeds):
-        """One-rank fold with stage 0 on one stream and stage 1 on another.
-        Order constraints: a stage's chunks run in order on its stream (the KV
-        history of chunk j + 1 is written by chunk j); stage 1 of chunk j waits
-        for stage 0 of chunk j (the fold pair); stage 0 of chunk j waits for
-        stage 1 of chunk j - 3 (the last reader of the pair it overwrites).
-        The caller's stream waits for both at the end."""
+        """The folded order with this rank's first-traversal stage (r) on one
+        stream and its second-traversal stage (2G-1-r) on another.  Order
+        constraints: a stage's chunks run in order on its stream (the KV
+        history of chunk j + 1 is written by chunk j); a boundary input is an
+        event wait on the consuming stream (``transport.receive``, or for the
+        local fold on rank G-1 the event of stage G-1 on the same chunk);
+        the fold rotates over three pairs, stage G-1 of chunk j waiting for
+        stage G of chunk j - 3.  Transport slot events are recorded on the
+        stream of the stage that fills or drains the slot.  The caller's
+        stream waits for both at the end."""
+        G = self.ranks
+        last_stage = 2 * G - 1
+        local = {self.rank: 0, last_stage - self.rank: 1}
         ctxs = self._contexts()
         main = torch.cuda.current_stream(self.device)
         start = torch.cuda.Event()
         start.record(main)
         for st in self.streams:
             st.wait_event(start)
+        if self.transport is not None:
+            self.transport.set_order(self.order)
         done = {}
         for batch, stage in self.order:
             ch, ctx = self.chunks[batch], ctxs[batch]
-            st = self.streams[stage]
+            li = local[stage]
+            st, ws = self.streams[li], self.model.ws_sets[li]
             fh, fr = self.folds[batch % 3]
             with torch.cuda.stream(st):
                 if stage == 0:
-                    if batch >= 3:  # a KeyError here would mean an order that breaks the fold rotation
-                        st.wait_event(done[(batch - 3, 1)])
                     if host_embeds is not None:
                         hidden = host_embeds[ch.request][ch.start:ch.start + ch.rows].to(self.device,
                                                                                            non_blocking=True)
                     else:
                         hidden = embeds[ch.request][ch.start:ch.start + ch.rows]
-                    self.model.run_layers(L.stage_layers(0, 1, self.shape.layers), hidden, None, ctx,
-                                          (fh[:ch.rows], fr[:ch.rows]), None, self.model.ws_sets[0])
+                    residual = None
+                elif stage == G:  # local fold: stage G-1 of this chunk ran on this rank
+                    st.wait_event(done[(batch, G - 1)])
+                    hidden, residual = fh[:ch.rows], fr[:ch.rows]
                 else:
-                    st.wait_event(done[(batch, 0)])
-                    h, r = self.model.run_layers(L.stage_layers(1, 1, self.shape.layers), fh[:ch.rows],
-                                                 fr[:ch.rows], ctx, None, None, self.model.ws_sets[1])
+                    hidden, residual = self.transport.receive(batch, stage, ch.rows)
+                on_residual = None
+                if stage == G - 1:
+                    if batch >= 3:  # a KeyError here would mean an order that breaks the fold rotation
+                        st.wait_event(done[(batch - 3, G)])
+                    out_planes = (fh[:ch.rows], fr[:ch.rows])
+                elif stage == last_stage:
+                    out_planes = None
+                else:
+                    out_planes = self.transport.prepare_send(batch, stage, ch.rows)
+                    on_residual = (lambda b=batch, s=stage: self.transport.mark_residual_ready(b, s))
+                h, r = self.model.run_layers(L.stage_layers(stage, G, self.shape.layers), hidden, residual, ctx,
+                                             out_planes, on_residual, ws)
+                if stage != last_stage and stage != G - 1:
+                    self.transport.send(batch, stage, ch.rows)
+                if stage != 0 and stage != G:
+                    self.transport.retire(batch, stage)
+                if stage == last_stage:
                     if self.keep_all_outputs:
                         self.outputs[batch] = self.model.final_norm(h, r)
                     if ch.start + ch.rows == self.request_tokens[ch.request]:
@@ -200,9 +229,10 @@ class FoldedRank:
                 ev = torch.cuda.Event()
                 ev.record(st)
                 done[(batch, stage)] = ev
-        with torch.cuda.stream(self.streams[1]):
-            # P+1: the one output token of every request (greedy), part of the bank.
-            self.model.sample(self.last_hidden, tokens=self.last_tokens)
+        if self.rank == self.output_rank:
+            with torch.cuda.stream(self.streams[local[last_stage]]):
+                # P+1: the one output token of every request (greedy), part of the bank.
+                self.model.sample(self.last_hidden, tokens=self.last_tokens)
         for st in self.streams:
             main.wait_stream(st)
         return self.last_hidden
