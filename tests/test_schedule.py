@@ -78,6 +78,22 @@ def test_orders_preserve_stage_fifo_and_dependencies(ranks, size):
     assert all(pos[r] == len(orders[r]) for r in range(ranks))
 
 
+@pytest.mark.parametrize("ranks", [1, 2, 4, 8])
+@pytest.mark.parametrize("size", [1, 3, 4, 15, 16, 40, 64])
+def test_orders_fit_the_overlapped_fold_rotation(ranks, size):
+    """The overlapped runner rotates the local fold over three buffer pairs:
+    on rank G-1, stage G-1 of chunk j overwrites the pair stage G of chunk
+    j - 3 read, so that read must already be issued (it then waits on its
+    event).  Every rank order must also issue stage G of a chunk after
+    stage G-1 of it (the event it waits on)."""
+    orders = L.rank_local_stage_orders(list(range(size)), ranks)
+    pos = {op: i for i, op in enumerate(orders[ranks - 1])}
+    for b in range(size):
+        assert pos[(b, ranks)] > pos[(b, ranks - 1)]
+        if b >= 3:
+            assert pos[(b - 3, ranks)] < pos[(b, ranks - 1)]
+
+
 @pytest.mark.parametrize("ranks", [2, 4, 8])
 def test_admission_bound_and_double_release(ranks):
     order = L.RankLocalOrder(0, ranks)
