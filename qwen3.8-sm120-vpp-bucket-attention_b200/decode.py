@@ -9,10 +9,12 @@ per-layer partials, semaphores and output, ``bind()`` validates the views and
 fixes the launch parameters, ``run()`` = ``assign()`` + ``compute()``.  The
 route rule choosing the task mode follows
 ``kernels/nvfp4_kv_bucket_worker.py:9-51``.  Differences: this build's cache
-(16-token pages, [pages, page, Hkv, D/2] codes, head_dim 128, any Hkv with up
-to 16 query heads per KV head) instead of the reference's 32-token pages with
-one KV head of 256; the dequantisation multipliers are the cache's fp32
-globals; there is no CPU path.
+(16-token pages, any power of two accepted; [pages, page, Hkv, D/2] codes in
+32-byte aligned rows, head_dim 128, any Hkv with up to 16 query heads per KV
+head) instead of the reference's 32-token pages with one KV head of 256; the
+dequantisation multipliers are the cache's fp32 globals; q K^T is formed from
+q written as four NVFP4 terms (relative error ~7e-5 of the group's largest
+query value); there is no CPU path.
 """
 
 import ctypes as ct
@@ -91,6 +93,8 @@ class TaskPlan:
 
     def __init__(self, batch, *, ctas, page_size=16, device="cuda"):
         _check_batch(batch, ctas)
+        if type(page_size) is not int or page_size < 1 or page_size & (page_size - 1):
+            raise ValueError("the decode kernel takes pages of a power-of-two token count")
         self.batch, self.ctas, self.page_size = batch, ctas, page_size
         self.capacity = ctas + batch - 1
         self.tasks = torch.empty((self.capacity, 4), dtype=torch.int32, device=device)

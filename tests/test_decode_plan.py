@@ -109,3 +109,11 @@ def test_query_terms_reconstruct_the_group(scale):
     assert errs[-1] < 2e-4
     zero = OD.q_terms(np.zeros((4, 128), np.float32))
     assert all(ig == 0.0 and not t.any() for t, ig in zero)
+
+
+@pytest.mark.parametrize("page_size", [0, 3, 24, 48])
+def test_plan_rejects_pages_that_are_not_a_power_of_two(page_size):
+    from qwen_infra_b200.decode import TaskPlan
+
+    with pytest.raises(ValueError):
+        TaskPlan(4, ctas=8, page_size=page_size, device="cpu")
