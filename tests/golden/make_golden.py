@@ -1,7 +1,7 @@
 """Regenerate the golden fixtures recorded from the reference project itself.
 
-Needs the reference checkout (read-only) at $QVPP_REFERENCE (default
-/root/reference) and, for the wire headers, the reference C++ sources
+Needs the reference checkout (read-only) at $QVPP_REFERENCE (the default
+is the REF path below) and, for the wire headers, the reference C++ sources
 compiled by ``oracle/build_ref.py``.  The committed JSON fixtures are what the
 tests read; this script is only how they were made.
 
