@@ -244,7 +244,8 @@ class StageModel:
         slots = bt[(pos // s.page_size).long()] * s.page_size + pos % s.page_size
         return ChunkContext(request, history, rows, pos, slots.to(torch.int32), bt)
 
-    def layer_forward(self, layer, hidden, residual, ctx, hidden_out, residual_out, on_residual=None, ws=None):
+    def layer_forward(self, layer, hidden, residual, ctx, hidden_out, residual_out, on_residual=None, ws=None,
+                      split=True):
         s, w = self.shape, self.weights[layer]
         ws = ws or self.ws
         rows = ctx.rows
@@ -268,7 +269,8 @@ class StageModel:
             K.kv_dequant(kv, ctx.block_table, tokens, k_out=kd, vt_out=vt)
         att = K.prefill_attention(q, kd, vt, history=ctx.history, qheads=s.qheads, kvheads=s.kvheads, head_dim=d,
                                   k_global=self.kg, v_global=self.vg, out=ws.att[:rows],
-                                  softmax_scale=self.softmax_scale, status=ws.status, workspace=ws.attn_ws)
+                                  softmax_scale=self.softmax_scale, status=ws.status,
+                                  workspace=ws.attn_ws if split else ws.attn_ws[:0])
         if self.kv_shadow and tokens >= self.request_tokens[ctx.request]:
             del self.shadow[(ctx.request, layer)]  # last chunk: stream order keeps the buffers until read
         a8, s8 = K.gate_fp8(att, qkv[:, d:], fp8=ws.a8[:rows], scale=ws.s8[:rows], head_dim=d, head_stride=2 * d)
@@ -285,11 +287,13 @@ class StageModel:
                      out=hidden_out)
         return hidden_out, residual_out
 
-    def run_layers(self, span, hidden, residual, ctx, out_planes=None, on_residual=None, ws=None):
+    def run_layers(self, span, hidden, residual, ctx, out_planes=None, on_residual=None, ws=None, split=True):
         """Run layers [lo, hi) on one chunk.  ``out_planes`` = (hidden, residual)
         buffers that receive the final layer's output (e.g. a transport slot).
         ``ws``: the workspace set (default the first); stages that run
-        concurrently need different ones."""
+        concurrently need different ones.  ``split=False``: no key-range split
+        of the attention's last partial wave (when another stream fills those
+        SMs, the split's extra CTAs and merge cost more than they save)."""
         lo, hi = span
         rows = ctx.rows
         ws = ws or self.ws
@@ -301,7 +305,7 @@ class StageModel:
             else:
                 ho, ro = ping[2 * (i % 2)], ping[2 * (i % 2) + 1]
             hidden, residual = self.layer_forward(layer, hidden, residual, ctx, ho, ro,
-                                                  on_residual if last else None, ws)
+                                                  on_residual if last else None, ws, split)
         return hidden, residual
 
     def final_norm(self, hidden, residual, out=None):

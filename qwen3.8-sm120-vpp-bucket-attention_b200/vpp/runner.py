@@ -173,8 +173,10 @@ class FoldedRank:
         local fold on rank G-1 the event of stage G-1 on the same chunk);
         the fold rotates over three pairs, stage G-1 of chunk j waiting for
         stage G of chunk j - 3.  Transport slot events are recorded on the
-        stream of the stage that fills or drains the slot.  The caller's
-        stream waits for both at the end."""
+        stream of the stage that fills or drains the slot.  The attention
+        runs without its key-range split here (the other stream fills the
+        last wave's idle SMs).  The caller's stream waits for both at the
+        end."""
         G = self.ranks
         last_stage = 2 * G - 1
         local = {self.rank: 0, last_stage - self.rank: 1}
@@ -216,7 +218,7 @@ class FoldedRank:
                     out_planes = self.transport.prepare_send(batch, stage, ch.rows)
                     on_residual = (lambda b=batch, s=stage: self.transport.mark_residual_ready(b, s))
                 h, r = self.model.run_layers(L.stage_layers(stage, G, self.shape.layers), hidden, residual, ctx,
-                                             out_planes, on_residual, ws)
+                                             out_planes, on_residual, ws, split=False)
                 if stage != last_stage and stage != G - 1:
                     self.transport.send(batch, stage, ch.rows)
                 if stage != 0 and stage != G:
