@@ -1,108 +1,110 @@
 #include "slot_pool.h"
 
-#include <algorithm>
 #include <atomic>
 
 namespace qvpp {
 namespace {
 
-std::atomic<std::uint64_t> g_next_ring{1};
+std::atomic<std::uint64_t> g_ring_ids{1};
 
-void need(bool ok, const char* what) {
-  if (!ok) throw SlotError(what);
-}
+[[noreturn]] void refuse(const char* why) { throw SlotError(why); }
 
-bool same_ticket(const Ticket& a, const Ticket& b) {
-  return a.ring_id == b.ring_id && a.sequence == b.sequence && a.generation == b.generation &&
-         a.slot_id == b.slot_id;
-}
+// One legal move: the state the slot must be in, the state it goes to, and
+// whether the ring must have been stopped first.
+struct Move {
+  bool allowed;
+  SlotState from, to;
+  bool only_when_stopped;
+};
+constexpr Move kNone{false, SlotState::Free, SlotState::Free, false};
+constexpr Move mv(SlotState from, SlotState to, bool stopped = false) { return Move{true, from, to, stopped}; }
+
+// kMoves[event][side]: side 0 = source, 1 = destination.
+constexpr Move kMoves[kSlotEvents][2] = {
+    /* Produced       */ {mv(SlotState::Reserved, SlotState::Produced), kNone},
+    /* TransferIssued */ {mv(SlotState::Produced, SlotState::Transferring),
+                          mv(SlotState::Reserved, SlotState::Transferring)},
+    /* ConsumerIssued */ {kNone, mv(SlotState::Transferring, SlotState::Consuming)},
+    /* SourceReadDone */ {mv(SlotState::Transferring, SlotState::Free), kNone},
+    /* ConsumerDone   */ {kNone, mv(SlotState::Consuming, SlotState::Free)},
+    /* Discarded      */ {kNone, mv(SlotState::Transferring, SlotState::Free)},
+    /* Abandoned      */ {mv(SlotState::Reserved, SlotState::Free, true),
+                          mv(SlotState::Reserved, SlotState::Free, true)},
+};
 
 }  // namespace
 
-PhysicalLeases::PhysicalLeases(std::uint32_t slots) : slots_(slots) {
-  need(slots >= 1 && slots <= owner_.size(), "invalid physical arena capacity");
+// ---- LeaseArena -------------------------------------------------------------
+
+LeaseArena::LeaseArena(std::uint32_t capacity)
+    : capacity_(capacity), full_mask_(capacity >= 1 && capacity <= kMaxSlots ? (1u << capacity) - 1u : 0u) {
+  if (capacity < 1 || capacity > kMaxSlots) refuse("a lease arena holds 1 to 7 physical slots");
 }
 
-std::uint32_t PhysicalLeases::acquire(const Ticket& t) {
-  need(available(), "physical arena has no free lease");
-  for (const auto& o : owner_)
-    need(!o || o->ring_id != t.ring_id || o->slot_id != t.slot_id, "logical ticket already has a physical lease");
-  for (std::uint32_t i = 0; i < slots_; ++i) {
-    if (!owner_[i]) {
-      owner_[i] = t;
-      ++live_;
-      peak_ = std::max(peak_, live_);
-      return i;
-    }
+std::uint32_t LeaseArena::acquire(const Ticket& t) {
+  if (!available()) refuse("every physical slot of the arena is leased");
+  for (std::uint32_t bits = busy_mask_; bits; bits &= bits - 1) {
+    const Ticket& h = holder_[__builtin_ctz(bits)];
+    if (h.ring_id == t.ring_id && h.slot_id == t.slot_id) refuse("this logical slot already holds a physical lease");
   }
-  throw std::logic_error("physical lease accounting mismatch");
+  const std::uint32_t physical = __builtin_ctz(~busy_mask_);  // lowest free slot
+  busy_mask_ |= 1u << physical;
+  holder_[physical] = t;
+  use_.up();
+  return physical;
 }
 
-void PhysicalLeases::release(std::uint32_t physical, const Ticket& t) {
-  need(physical < slots_, "physical lease outside arena");
-  need(owner_[physical].has_value() && same_ticket(*owner_[physical], t),
-       "physical lease completion belongs to another ticket/generation");
-  owner_[physical].reset();
-  --live_;
+void LeaseArena::release(std::uint32_t physical, const Ticket& t) {
+  if (physical >= capacity_) refuse("physical slot index past the arena");
+  if (!(busy_mask_ >> physical & 1u) || !(holder_[physical] == t))
+    refuse("lease returned by a ticket that does not hold it");
+  busy_mask_ &= ~(1u << physical);
+  use_.down();
 }
 
-SlotRing::SlotRing(Role role, Layout layout, std::uint64_t epoch, std::uint32_t src_stage)
-    : role_(role), layout_(layout), epoch_(epoch), id_(g_next_ring.fetch_add(1)), src_stage_(src_stage) {
-  make_boundary(layout_, epoch_, 0, 0, src_stage_, 0);  // validates epoch, edge and layout
-  need(role == Role::Source || role == Role::Destination, "invalid pool role");
+// ---- SlotRing ---------------------------------------------------------------
+
+SlotRing::SlotRing(Role side, Layout layout, std::uint64_t epoch, std::uint32_t src_stage)
+    : side_(side), layout_(layout), epoch_(epoch), ring_id_(g_ring_ids.fetch_add(1)), src_stage_(src_stage) {
+  if (side != Role::Source && side != Role::Destination) refuse("ring side must be source or destination");
+  make_boundary(layout_, epoch_, 0, 0, src_stage_, 0);  // checks the layout, epoch and edge
 }
 
 std::optional<Ticket> SlotRing::try_acquire(const Boundary& d) {
-  need(!stopped_, "role stopped; create a new role epoch, do not resume");
+  if (stopped_) refuse("ring was stopped; a new epoch needs a new ring");
   validate_boundary(layout_, d);
-  need(d.epoch == epoch_ && d.src_stage == src_stage_, "wrong role epoch or edge");
-  need(d.edge_sequence == next_, "out-of-order boundary admission");
-  Entry& e = entries_[d.slot_id];
-  if (e.state != SlotState::Free) return std::nullopt;
-  e.desc = d;
-  e.state = SlotState::Reserved;
-  ++next_;
-  ++live_;
-  peak_ = std::max(peak_, live_);
-  return Ticket{id_, d.edge_sequence, d.generation, d.slot_id};
+  if (d.epoch != epoch_ || d.src_stage != src_stage_) refuse("message belongs to another epoch or edge");
+  if (d.edge_sequence != expected_) refuse("message admitted out of edge-sequence order");
+  Record& r = slots_[d.slot_id];
+  if (r.state != SlotState::Free) return std::nullopt;
+  r.desc = d;
+  r.state = SlotState::Reserved;
+  ++expected_;
+  use_.up();
+  return Ticket{ring_id_, d.edge_sequence, d.generation, d.slot_id};
 }
 
-const SlotRing::Entry& SlotRing::entry(const Ticket& t) const {
-  need(t.ring_id == id_ && t.slot_id < layout_.slot_count, "ticket belongs to another pool");
-  const Entry& e = entries_[t.slot_id];
-  need(e.state != SlotState::Free && e.desc.edge_sequence == t.sequence && e.desc.generation == t.generation,
-       "stale completion or retired ticket");
-  return e;
+SlotRing::Record& SlotRing::locate(const Ticket& t) {
+  if (t.ring_id != ring_id_ || t.slot_id >= layout_.slot_count) refuse("ticket was issued by another ring");
+  Record& r = slots_[t.slot_id];
+  if (r.state == SlotState::Free || r.desc.edge_sequence != t.sequence || r.desc.generation != t.generation)
+    refuse("ticket no longer names a live message (retired or older generation)");
+  return r;
 }
 
-const Boundary& SlotRing::descriptor(const Ticket& t) const { return entry(t).desc; }
-SlotState SlotRing::state(const Ticket& t) const { return entry(t).state; }
+const Boundary& SlotRing::descriptor(const Ticket& t) const { return locate(t).desc; }
+SlotState SlotRing::state(const Ticket& t) const { return locate(t).state; }
 
-void SlotRing::move(const Ticket& t, Role required, SlotState from, SlotState to) {
-  need(role_ == required && entry(t).state == from, "invalid slot transition");
-  entries_[t.slot_id].state = to;
-  if (to == SlotState::Free) --live_;
-}
-
-void SlotRing::producer_recorded(const Ticket& t) { move(t, Role::Source, SlotState::Reserved, SlotState::Produced); }
-void SlotRing::transfer_recorded(const Ticket& t) {
-  move(t, role_, role_ == Role::Source ? SlotState::Produced : SlotState::Reserved, SlotState::Transferring);
-}
-void SlotRing::consumer_recorded(const Ticket& t) {
-  move(t, Role::Destination, SlotState::Transferring, SlotState::Consuming);
-}
-void SlotRing::source_read_complete(const Ticket& t) {
-  move(t, Role::Source, SlotState::Transferring, SlotState::Free);
-}
-void SlotRing::consumer_complete(const Ticket& t) {
-  move(t, Role::Destination, SlotState::Consuming, SlotState::Free);
-}
-void SlotRing::discard_received(const Ticket& t) {
-  move(t, Role::Destination, SlotState::Transferring, SlotState::Free);
-}
-void SlotRing::release_unsubmitted(const Ticket& t) {
-  need(stopped_, "unsent sequence can only be abandoned at fatal role shutdown");
-  move(t, role_, SlotState::Reserved, SlotState::Free);
+void SlotRing::apply(const Ticket& t, SlotEvent ev) {
+  const int e = static_cast<int>(ev);
+  if (e < 0 || e >= kSlotEvents) refuse("unknown slot event");
+  const Move& m = kMoves[e][side_ == Role::Source ? 0 : 1];
+  if (!m.allowed) refuse("event does not apply to this side of the edge");
+  if (m.only_when_stopped && !stopped_) refuse("a reserved message may be abandoned only after the ring stopped");
+  Record& r = locate(t);
+  if (r.state != m.from) refuse("event does not apply in the slot's current state");
+  r.state = m.to;
+  if (m.to == SlotState::Free) use_.down();
 }
 
 }  // namespace qvpp

@@ -181,23 +181,12 @@ int qv_ring_try_acquire(void* r, const QvBoundaryC* d, QvTicketC* out) {
   }
 }
 
-// op: 0 producer_recorded, 1 transfer_recorded, 2 consumer_recorded,
-//     3 source_read_complete, 4 consumer_complete, 5 discard_received,
-//     6 release_unsubmitted
+// op: a SlotEvent value (0 produced, 1 transfer issued, 2 consumer issued,
+//     3 source read done, 4 consumer done, 5 discarded, 6 abandoned)
 int qv_ring_transition(void* r, const QvTicketC* t, int op) {
   try {
-    auto* ring = static_cast<SlotRing*>(r);
-    const Ticket tk = ticket_from(t);
-    switch (op) {
-      case 0: ring->producer_recorded(tk); break;
-      case 1: ring->transfer_recorded(tk); break;
-      case 2: ring->consumer_recorded(tk); break;
-      case 3: ring->source_read_complete(tk); break;
-      case 4: ring->consumer_complete(tk); break;
-      case 5: ring->discard_received(tk); break;
-      case 6: ring->release_unsubmitted(tk); break;
-      default: throw SlotError("unknown slot transition");
-    }
+    if (op < 0 || op >= kSlotEvents) throw SlotError("unknown slot event");
+    static_cast<SlotRing*>(r)->apply(ticket_from(t), SlotEvent(op));
     return 0;
   } catch (const std::exception& e) {
     return fail(e);
@@ -229,33 +218,33 @@ std::uint64_t qv_ring_next_sequence(void* r) { return static_cast<SlotRing*>(r)-
 // ---- physical leases --------------------------------------------------------
 void* qv_leases_create(std::uint32_t slots) {
   try {
-    return new PhysicalLeases(slots);
+    return new LeaseArena(slots);
   } catch (const std::exception& e) {
     fail(e);
     return nullptr;
   }
 }
-void qv_leases_destroy(void* l) { delete static_cast<PhysicalLeases*>(l); }
-int qv_leases_available(void* l) { return static_cast<PhysicalLeases*>(l)->available() ? 1 : 0; }
+void qv_leases_destroy(void* l) { delete static_cast<LeaseArena*>(l); }
+int qv_leases_available(void* l) { return static_cast<LeaseArena*>(l)->available() ? 1 : 0; }
 int qv_leases_acquire(void* l, const QvTicketC* t) {
   try {
-    return int(static_cast<PhysicalLeases*>(l)->acquire(ticket_from(t)));
+    return int(static_cast<LeaseArena*>(l)->acquire(ticket_from(t)));
   } catch (const std::exception& e) {
     return fail(e);
   }
 }
 int qv_leases_release(void* l, std::uint32_t physical, const QvTicketC* t) {
   try {
-    static_cast<PhysicalLeases*>(l)->release(physical, ticket_from(t));
+    static_cast<LeaseArena*>(l)->release(physical, ticket_from(t));
     return 0;
   } catch (const std::exception& e) {
     return fail(e);
   }
 }
-void qv_leases_note_stall(void* l) { static_cast<PhysicalLeases*>(l)->note_stall(); }
-std::uint32_t qv_leases_live(void* l) { return static_cast<PhysicalLeases*>(l)->live(); }
-std::uint32_t qv_leases_peak_live(void* l) { return static_cast<PhysicalLeases*>(l)->peak_live(); }
-std::uint64_t qv_leases_stalls(void* l) { return static_cast<PhysicalLeases*>(l)->stalls(); }
+void qv_leases_note_stall(void* l) { static_cast<LeaseArena*>(l)->note_stall(); }
+std::uint32_t qv_leases_live(void* l) { return static_cast<LeaseArena*>(l)->live(); }
+std::uint32_t qv_leases_peak_live(void* l) { return static_cast<LeaseArena*>(l)->peak_live(); }
+std::uint64_t qv_leases_stalls(void* l) { return static_cast<LeaseArena*>(l)->stalls(); }
 
 // ---- edge control pages -----------------------------------------------------
 void* qv_ctrl_create(const char* name) {

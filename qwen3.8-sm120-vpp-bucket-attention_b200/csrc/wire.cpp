@@ -27,7 +27,7 @@ std::uint64_t load_le(const Wire& w, std::size_t at, unsigned n) {
 }  // namespace
 
 std::uint32_t Topology::stage_rank(std::uint32_t stage) const {
-  check(ranks >= 1 && stage < stages(), "invalid virtual stage");
+  check(ranks >= 1 && stage < stages(), "virtual stage index outside 0 .. 2G-1");
   return stage < ranks ? stage : stages() - 1 - stage;
 }
 
@@ -43,29 +43,29 @@ std::vector<std::uint32_t> Topology::source_stages() const {
 }
 
 std::uint32_t Topology::edge_index(std::uint32_t src, std::uint32_t dst) const {
-  check(is_wire_edge(src, dst), "not a remote folded edge");
+  check(is_wire_edge(src, dst), "stage pair is not a wire edge of the folded layout");
   return src < ranks ? src : src - 1;
 }
 
 void Layout::validate() const {
-  check(token_capacity > 0 && token_capacity <= 16384, "invalid token capacity");
-  check(slot_count > 0 && slot_count <= 7, "invalid admitted boundary capacity");
-  check(hidden > 0 && hidden % 8 == 0, "invalid hidden size");
-  check(topo.ranks >= 2 && topo.ranks <= 64, "invalid rank count");
+  check(token_capacity > 0 && token_capacity <= 16384, "slot token capacity must be 1 .. 16384");
+  check(slot_count > 0 && slot_count <= 7, "ring must hold 1 to 7 slots");
+  check(hidden > 0 && hidden % 8 == 0, "hidden size must be a positive multiple of 8");
+  check(topo.ranks >= 2 && topo.ranks <= 64, "rank count must be 2 .. 64");
 }
 
 void validate_boundary(const Layout& layout, const Boundary& d) {
   layout.validate();
   layout.topo.edge_index(d.src_stage, d.dst_stage);
-  check(d.epoch != 0, "role epoch must be nonzero");
+  check(d.epoch != 0, "epoch 0 is reserved");
   check(d.edge_sequence != std::numeric_limits<std::uint64_t>::max(),
-        "edge sequence exhausted; restart role epoch, never wrap");
-  check(d.slot_id == d.edge_sequence % layout.slot_count, "wrong ring slot");
-  check(d.generation == d.edge_sequence / layout.slot_count + 1, "wrong slot generation");
-  check(d.valid_tokens <= layout.token_capacity, "boundary exceeds capacity");
+        "edge sequence would overflow; start a new epoch (sequences never wrap)");
+  check(d.slot_id == d.edge_sequence % layout.slot_count, "slot id is not sequence mod ring size");
+  check(d.generation == d.edge_sequence / layout.slot_count + 1, "generation is not sequence / ring size + 1");
+  check(d.valid_tokens <= layout.token_capacity, "valid tokens exceed the slot capacity");
   const std::uint64_t bytes = std::uint64_t(d.valid_tokens) * layout.hidden * 2;
-  check(d.hidden.offset_bytes == 0 && d.hidden.valid_bytes == bytes, "invalid hidden span");
-  check(d.residual.offset_bytes == layout.plane_bytes() && d.residual.valid_bytes == bytes, "invalid residual span");
+  check(d.hidden.offset_bytes == 0 && d.hidden.valid_bytes == bytes, "hidden plane span does not match the layout");
+  check(d.residual.offset_bytes == layout.plane_bytes() && d.residual.valid_bytes == bytes, "residual plane span does not match the layout");
 }
 
 Boundary make_boundary(const Layout& layout, std::uint64_t epoch, std::int64_t batch, std::uint64_t sequence,
@@ -114,7 +114,7 @@ Wire encode_boundary(const Layout& layout, const Boundary& d) {
 Boundary decode_boundary(const Layout& layout, const Wire& w) {
   check(load_le(w, 0, 4) == kMagic && load_le(w, 4, 2) == kVersion && load_le(w, 6, 2) == kKindDualBf16 &&
             load_le(w, 88, 8) == 0,
-        "unsupported boundary wire header");
+        "wire header magic, version or kind not recognised");
   Boundary d;
   d.epoch = load_le(w, 8, 8);
   const std::uint64_t bits = load_le(w, 16, 8);
@@ -135,7 +135,7 @@ Boundary match_boundary(const Layout& layout, const Wire& w, std::uint64_t epoch
                         std::uint64_t sequence, std::uint32_t src) {
   Boundary d = decode_boundary(layout, w);
   check(d.epoch == epoch && d.batch_id == batch && d.edge_sequence == sequence && d.src_stage == src,
-        "boundary does not match the admitted stage identity");
+        "header names another epoch, batch, sequence or edge than expected");
   return d;
 }
 

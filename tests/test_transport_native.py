@@ -138,6 +138,78 @@ def test_destination_lifecycle_and_discard():
     assert dst.live == 0 and dst.peak_live == 1 and dst.next_sequence == 2
 
 
+# Every (side, event, state) combination against the slot protocol: the
+# legal moves of a message's slot on each side of an edge
+# (src/qwen_infra/vpp/native/slot_pool.h:9-75); everything else is refused
+# and leaves the slot where it was.
+_LEGAL = {
+    ("source", NV.OP_PRODUCER_RECORDED, "reserved"): "produced",
+    ("source", NV.OP_TRANSFER_RECORDED, "produced"): "transferring",
+    ("source", NV.OP_SOURCE_READ_COMPLETE, "transferring"): "free",
+    ("destination", NV.OP_TRANSFER_RECORDED, "reserved"): "transferring",
+    ("destination", NV.OP_CONSUMER_RECORDED, "transferring"): "consuming",
+    ("destination", NV.OP_CONSUMER_COMPLETE, "consuming"): "free",
+    ("destination", NV.OP_DISCARD_RECEIVED, "transferring"): "free",
+}
+_PATH = {"source": [NV.OP_PRODUCER_RECORDED, NV.OP_TRANSFER_RECORDED],
+         "destination": [NV.OP_TRANSFER_RECORDED, NV.OP_CONSUMER_RECORDED]}
+
+
+@pytest.mark.parametrize("side", ["source", "destination"])
+def test_every_slot_event_in_every_state(side):
+    lay = NV.BoundaryLayout(256, 3, 2, 256)
+    role = NV.SOURCE if side == "source" else NV.DESTINATION
+    for depth in range(3):  # reserved, then one and two steps along the side's path
+        for op in range(7):
+            ring = NV.SlotRing(role, lay, 2, 0)
+            t = ring.try_acquire(lay.make(2, 0, 0, 0, 8))
+            for step in _PATH[side][:depth]:
+                ring.transition(t, step)
+            before = ring.state(t)
+            want = _LEGAL.get((side, op, before))
+            if want is None:
+                with pytest.raises(NV.BoundaryError):
+                    ring.transition(t, op)
+                assert ring.state(t) == before and ring.live == 1
+            else:
+                ring.transition(t, op)
+                if want == "free":
+                    assert ring.live == 0
+                    with pytest.raises(NV.BoundaryError):
+                        ring.state(t)
+                else:
+                    assert ring.state(t) == want
+    # abandoning a reserved message is legal on both sides, after stop() only
+    ring = NV.SlotRing(role, lay, 2, 0)
+    t = ring.try_acquire(lay.make(2, 0, 0, 0, 8))
+    with pytest.raises(NV.BoundaryError):
+        ring.transition(t, NV.OP_RELEASE_UNSUBMITTED)
+    ring.stop()
+    ring.transition(t, NV.OP_RELEASE_UNSUBMITTED)
+    assert ring.live == 0
+
+
+def test_lease_arena_capacity_and_lowest_free_slot():
+    for bad in (0, 8):
+        with pytest.raises(NV.BoundaryError):
+            NV.PhysicalLeases(bad)
+    lay = NV.BoundaryLayout(256, 7, 2, 256)
+    leases = NV.PhysicalLeases(3)
+    ring = NV.SlotRing(NV.SOURCE, lay, 2, 0)
+    ts = [ring.try_acquire(lay.make(2, s, s, 0, 8)) for s in range(3)]
+    got = [leases.acquire(t) for t in ts]
+    assert got == [0, 1, 2] and not leases.available
+    leases.release(1, ts[1])
+    t3 = NV.QvTicket(ts[1].ring_id, 99, 99, 5)
+    assert leases.acquire(t3) == 1  # the lowest free physical slot is reused
+    with pytest.raises(NV.BoundaryError):
+        leases.acquire(ts[0])  # arena full
+    leases.release(0, ts[0])
+    with pytest.raises(NV.BoundaryError):
+        leases.acquire(ts[2])  # logical slot 2 already holds physical slot 2
+    assert leases.peak_live == 3
+
+
 def test_reference_known_answer_binary_when_built():
     exe = REPO / "oracle/_ref/slot_pool_test"
     if not exe.exists():
