@@ -678,19 +678,24 @@ int launch_attention(const QiAttention* a, cudaStream_t stream) {
 
 }  // namespace
 
-extern "C" int qi_prefill_attention(const QiAttention* a, cudaStream_t stream) {
-  QI_BIND(stream, a ? a->q : nullptr);
+namespace qi {
+bool attention_request_valid(const QiAttention* a) {
   if (!a || a->rows < 1 || a->history < 0 || (a->head_dim != 64 && a->head_dim != 128) || a->qheads < 1 ||
       a->kvheads < 1 || a->qheads % a->kvheads || !a->q || !a->k || !a->vt || !a->out || !a->k_global ||
       !a->v_global)
-    return (int)cudaErrorInvalidValue;
+    return false;
   const int64_t hd = a->head_dim;
   if (a->kv_tokens < a->history + a->rows || a->vt_row < a->kv_tokens || a->vt_row % 8 || a->q_row % 8 ||
       a->out_row % 8 || a->q_row < a->qheads * hd || a->out_row < a->qheads * hd)
-    return (int)cudaErrorInvalidValue;
-  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->vt) || !aligned16(a->out) ||
-      (a->workspace && (reinterpret_cast<uintptr_t>(a->workspace) & 255)))
-    return (int)cudaErrorInvalidValue;
+    return false;
+  return aligned16(a->q) && aligned16(a->k) && aligned16(a->vt) && aligned16(a->out) &&
+         !(a->workspace && (reinterpret_cast<uintptr_t>(a->workspace) & 255));
+}
+}  // namespace qi
+
+extern "C" int qi_prefill_attention(const QiAttention* a, cudaStream_t stream) {
+  QI_BIND(stream, a ? a->q : nullptr);
+  if (!attention_request_valid(a)) return (int)cudaErrorInvalidValue;
   return a->head_dim == 64 ? launch_attention<64>(a, stream) : launch_attention<128>(a, stream);
 }
 

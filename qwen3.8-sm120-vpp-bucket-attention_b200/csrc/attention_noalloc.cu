@@ -91,10 +91,6 @@ extern "C" int qi_paged_prefill_attention_noalloc(const QiKvView* kv, const int3
   e = scratch_address(device, &scratch, &split);
   if (e != cudaSuccess) return (int)e;
   unsigned char* base = static_cast<unsigned char*>(scratch);
-  e = cudaMemsetAsync(split, 0, 4096, stream);  // arrival counters of the split units
-  if (e != cudaSuccess) return (int)e;
-  int rc = qi_kv_dequant(kv, block_table, (int)tokens, base, base + k_span, vt_row, stream);
-  if (rc) return rc;
   QiAttention a{};
   a.q = q;
   a.k = base;
@@ -115,5 +111,15 @@ extern "C" int qi_paged_prefill_attention_noalloc(const QiKvView* kv, const int3
   a.softmax_scale = softmax_scale;
   a.workspace = split;
   a.workspace_bytes = (int64_t)kSplitBytes;
+  // Check both launches' arguments before touching the shared array: a
+  // rejected call must not overwrite scratch that an earlier call may still
+  // be reading.
+  if (!qi::kv_dequant_request_valid(kv, block_table, 0, (int)tokens, a.k, tokens, a.vt, vt_row) ||
+      !qi::attention_request_valid(&a))
+    return (int)cudaErrorInvalidValue;
+  e = cudaMemsetAsync(split, 0, 4096, stream);  // arrival counters of the split units
+  if (e != cudaSuccess) return (int)e;
+  int rc = qi_kv_dequant(kv, block_table, (int)tokens, base, base + k_span, vt_row, stream);
+  if (rc) return rc;
   return qi_prefill_attention(&a, stream);
 }

@@ -8,6 +8,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "qwen_infra_b200.h"
+
 #define QI_DEV __device__ __forceinline__
 
 namespace qi {
@@ -376,5 +378,12 @@ QI_DEV bool elect_one() {
       : "=r"(pred));
   return pred != 0;
 }
+
+// Host-side request checks shared by entry points that combine several
+// launches (the allocation-free attention): every argument is checked before
+// the first launch, so a rejected call launches nothing.
+bool attention_request_valid(const QiAttention* a);
+bool kv_dequant_request_valid(const QiKvView* kv, const int32_t* block_table, int first, int tokens,
+                              const void* k_out, int64_t k_capacity, const void* vt_out, int64_t vt_row);
 
 }  // namespace qi

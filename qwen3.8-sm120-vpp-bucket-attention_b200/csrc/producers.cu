@@ -470,6 +470,23 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 
 }  // namespace
 
+namespace qi {
+bool kv_dequant_request_valid(const QiKvView* kv, const int32_t* block_table, int first, int tokens,
+                              const void* k_out, int64_t k_capacity, const void* vt_out, int64_t vt_row) {
+  if (!kv || !block_table || tokens < 1 || first < 0 || first % 64 || first >= tokens || !k_out || !vt_out ||
+      k_capacity < tokens || vt_row < tokens || vt_row % 64)
+    return false;
+  if (!kv->k_cache || !kv->v_cache || !kv->k_scales || !kv->v_scales || kv->kvheads < 1 || kv->page_size < 1 ||
+      (kv->head_dim != 64 && kv->head_dim != 128))
+    return false;
+  // 16-byte code loads and 2-byte scale loads per 32 values of a token
+  return aligned16(kv->k_cache) && aligned16(kv->v_cache) && !(kv->data_page % 16) && !(kv->data_row % 16) &&
+         !(kv->data_head % 16) && !(reinterpret_cast<uintptr_t>(kv->k_scales) & 1) &&
+         !(reinterpret_cast<uintptr_t>(kv->v_scales) & 1) && !(kv->sf_page % 2) && !(kv->sf_row % 2) &&
+         !(kv->sf_head % 2) && aligned16(k_out) && aligned16(vt_out);
+}
+}  // namespace qi
+
 extern "C" {
 
 int qi_norm_pack(const void* x, const void* residual, const void* gamma, const float* global_scale, void* q,
@@ -675,16 +692,7 @@ int qi_fp8_quantize_rows(const float* w, int rows, int k, void* q, float* scales
 int qi_kv_dequant_range(const QiKvView* kv, const int32_t* block_table, int first, int tokens, void* k_out,
                         int64_t k_capacity, void* vt_out, int64_t vt_row, cudaStream_t stream) {
   QI_BIND(stream, k_out);
-  if (!kv || !block_table || tokens < 1 || first < 0 || first % 64 || first >= tokens || !k_out || !vt_out ||
-      k_capacity < tokens || vt_row < tokens || vt_row % 64)
-    return (int)cudaErrorInvalidValue;
-  if (!kv->k_cache || !kv->v_cache || !kv->k_scales || !kv->v_scales || kv->kvheads < 1 || kv->page_size < 1)
-    return (int)cudaErrorInvalidValue;
-  // 16-byte code loads and 2-byte scale loads per 32 values of a token
-  if (!aligned16(kv->k_cache) || !aligned16(kv->v_cache) || kv->data_page % 16 || kv->data_row % 16 ||
-      kv->data_head % 16 || (reinterpret_cast<uintptr_t>(kv->k_scales) & 1) ||
-      (reinterpret_cast<uintptr_t>(kv->v_scales) & 1) || kv->sf_page % 2 || kv->sf_row % 2 || kv->sf_head % 2 ||
-      !aligned16(k_out) || !aligned16(vt_out))
+  if (!kv_dequant_request_valid(kv, block_table, first, tokens, k_out, k_capacity, vt_out, vt_row))
     return (int)cudaErrorInvalidValue;
   const dim3 grid((tokens - first + 63) / 64, kv->kvheads);
   const int64_t ks = k_capacity * kv->head_dim, vs = (int64_t)kv->head_dim * vt_row;

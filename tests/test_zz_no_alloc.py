@@ -58,11 +58,17 @@ def test_noalloc_attention_matches_two_call_path_twice(first, second):
                                    v_global=vg)
         got = torch.full_like(want, float("nan"))
         view = kv.view()
+        torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info(dev)[0]
         rc = fn(ct.byref(view), ct.c_void_p(table.data_ptr()), ct.c_void_p(q.data_ptr()), q.stride(0),
                 ct.c_void_p(got.data_ptr()), got.stride(0), rows, history, qh, ct.c_void_p(kg.data_ptr()),
                 ct.c_void_p(vg.data_ptr()), 1.0 / math.sqrt(d), None, stream)
         assert rc == 0
         torch.cuda.synchronize()
+        if i == 1:
+            # the kernels' code is resident after the first call, so a call
+            # that allocates nothing leaves the device's free memory as it was
+            assert torch.cuda.mem_get_info(dev)[0] == free_before
         err = (got.float() - want.float()).abs().max().item() / want.float().abs().max().item()
         assert err < 2e-2, err  # the tolerance of the attention parity tests
         assert torch.equal(got, want)  # same kernels on the same values: identical in fact
