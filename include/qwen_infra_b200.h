@@ -131,6 +131,13 @@ int qi_gate_fp8(const void* out, const void* gate, int64_t out_row, int64_t gate
 int qi_gate_fp8_heads(const void* out, const void* gate, int64_t out_row, int64_t gate_row, int64_t gate_head_stride,
                       int head_dim, void* fp8, int64_t fp8_row, float* scale, int rows, int cols,
                       cudaStream_t stream);
+/* The reference's own form of the epilogue (store_final_fp8,
+ * nvfp4_bucket_xqa.cu:48-66): one static per-tensor scale read from the
+ * device scalar `scale`, fp8 = e4m3_satfinite(bf16(out * bf16(sigmoid(gate))) / scale);
+ * no per-token scale is written.  Gate addressing as qi_gate_fp8_heads. */
+int qi_gate_fp8_static(const void* out, const void* gate, int64_t out_row, int64_t gate_row,
+                       int64_t gate_head_stride, int head_dim, void* fp8, int64_t fp8_row, const float* scale,
+                       int rows, int cols, cudaStream_t stream);
 
 /* ---- tcgen05 GEMM: D[m, n] = A[m, k] . B[n, k]^T ------------------------ */
 #define QI_GEMM_NVFP4 0 /* kind::mxf4nvf4, E2M1 with 16-element E4M3 block scales */

@@ -92,6 +92,7 @@ EXPORTS = {
     "qi_qk_rope_kv_append_resources": ([ct.POINTER(_i32)], _i32),
     "qi_gate_fp8": ([_vp, _vp, _i64, _i64, _vp, _i64, _vp, _i32, _i32, _vp], _i32),
     "qi_gate_fp8_heads": ([_vp, _vp, _i64, _i64, _i64, _i32, _vp, _i64, _vp, _i32, _i32, _vp], _i32),
+    "qi_gate_fp8_static": ([_vp, _vp, _i64, _i64, _i64, _i32, _vp, _i64, _vp, _i32, _i32, _vp], _i32),
     "qi_gemm": ([ct.POINTER(QiGemm), _vp], _i32),
     "qi_gemm_resources": ([ct.POINTER(_i32)], _i32),
     "qi_kv_dequant": ([ct.POINTER(QiKvView), _vp, _i32, _vp, _vp, _i64, _vp], _i32),

@@ -10,6 +10,8 @@ Outputs are written next to this file so that they travel with the source tree.
 import os
 import shutil
 import subprocess
+import tempfile
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
@@ -53,15 +55,40 @@ def _run(argv, log):
         raise RuntimeError(f"build failed ({' '.join(map(str, argv[:3]))} ...): see {log}\n" + Path(log).read_text()[-4000:])
 
 
+# Extra flags per source.  The producers compile without FMA contraction, as
+# the reference builds its producer kernels (--fmad=false): their own fp32
+# steps are explicit IEEE operations either way, and the CUDA math functions
+# they call (rsqrtf, expf) are then compiled under the reference's setting.
+FILE_FLAGS = {"producers.cu": ["--fmad=false"]}
+
+
 def build_kernels(force=False):
     sources = [CSRC / s for s in KERNEL_SOURCES]
-    deps = sources + [CSRC / "common.cuh", INCLUDE / "qwen_infra_b200.h"]
+    deps = sources + [CSRC / "common.cuh", INCLUDE / "qwen_infra_b200.h", Path(__file__)]
     if not force and not _stale(KERNEL_LIB, deps):
         return KERNEL_LIB
     nvcc = cuda_home() / "bin" / "nvcc"
-    tmp = KERNEL_LIB.with_suffix(".part.so")
-    argv = [str(nvcc), *NVCC_FLAGS, "-I", str(INCLUDE), *map(str, sources), "-o", str(tmp)]
-    _run(argv, PKG / "build_kernels.log")
+    compile_flags = [f for f in NVCC_FLAGS if f not in ("--shared", "-cudart", "static")]
+    log = PKG / "build_kernels.log"
+    with tempfile.TemporaryDirectory(prefix="qi_build_") as tmpdir:
+        objs = [Path(tmpdir) / (s.stem + ".o") for s in sources]
+
+        def compile_one(i):
+            src = sources[i]
+            argv = [str(nvcc), *compile_flags, *FILE_FLAGS.get(src.name, []), "-I", str(INCLUDE), "-c", str(src),
+                    "-o", str(objs[i])]
+            return subprocess.run(argv, capture_output=True, text=True, timeout=900)
+
+        with ThreadPoolExecutor(max_workers=len(sources)) as pool:
+            results = list(pool.map(compile_one, range(len(sources))))
+        with open(log, "w") as out:
+            for src, r in zip(sources, results):
+                out.write(f"== {src.name} (rc {r.returncode})\n{r.stdout}{r.stderr}")
+        if any(r.returncode for r in results):
+            raise RuntimeError(f"kernel build failed: see {log}\n" + log.read_text()[-4000:])
+        tmp = KERNEL_LIB.with_suffix(".part.so")
+        _run([str(nvcc), "-gencode", "arch=compute_100a,code=sm_100a", "--shared", "-cudart", "static",
+              *map(str, objs), "-o", str(tmp)], PKG / "build_link.log")
     os.replace(tmp, KERNEL_LIB)
     return KERNEL_LIB
 

@@ -111,45 +111,11 @@ QI_DEV uint32_t f2_to_e2m1x2(float lo, float hi) {
   return out & 0xFFu;
 }
 
-// exp(x) = 2^n * 2^f with t = x*log2(e), n = rint(t), f = t - n in [-1/2, 1/2];
-// 2^f by its degree-6 Taylor polynomial in Horner form (coefficients
-// (ln 2)^k / k! rounded to fp32).  Every step is one IEEE fp32 operation so a
-// CPU restatement reproduces it bit for bit.
-constexpr float kLog2e = 0x1.715476p+0f;
-constexpr float kExpC6 = 0x1.430912p-13f;
-constexpr float kExpC5 = 0x1.5d87fep-10f;
-constexpr float kExpC4 = 0x1.3b2ab6p-7f;
-constexpr float kExpC3 = 0x1.c6b08ep-5f;
-constexpr float kExpC2 = 0x1.ebfbe0p-3f;
-constexpr float kExpC1 = 0x1.62e430p-1f;
-constexpr float kExpC0 = 1.0f;
-
-QI_DEV float fexp(float x) {
-  const float t = __fmul_rn(x, kLog2e);
-  if (t >= 128.0f) return __int_as_float(0x7f800000);
-  if (t <= -150.0f) return 0.0f;
-  const float tc = fminf(fmaxf(t, -149.0f), 127.0f);
-  // n = rint(tc): adding 1.5 * 2^23 leaves a unit last place, so the sum is tc
-  // rounded to the nearest integer (ties to even) and its low bits hold n; two
-  // FMA-pipe adds instead of the quarter-rate FRND / F2I conversions.
-  const float nb = __fadd_rn(tc, 12582912.0f);
-  const float n = __fsub_rn(nb, 12582912.0f);
-  const float f = __fsub_rn(tc, n);
-  float p = kExpC6;
-  p = __fadd_rn(__fmul_rn(p, f), kExpC5);
-  p = __fadd_rn(__fmul_rn(p, f), kExpC4);
-  p = __fadd_rn(__fmul_rn(p, f), kExpC3);
-  p = __fadd_rn(__fmul_rn(p, f), kExpC2);
-  p = __fadd_rn(__fmul_rn(p, f), kExpC1);
-  p = __fadd_rn(__fmul_rn(p, f), kExpC0);
-  const int ni = __float_as_int(nb) - 0x4B400000;
-  const int h1 = ni >> 1, h2 = ni - h1;
-  const float s1 = __int_as_float((h1 + 127) << 23), s2 = __int_as_float((h2 + 127) << 23);
-  return __fmul_rn(__fmul_rn(p, s1), s2);
-}
-
-QI_DEV float sigmoid_f(float g) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, fexp(-g))); }
-QI_DEV float silu_f(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, fexp(-g))); }
+// sigmoid and SiLU with CUDA's expf, as the reference calls it
+// (nvfp4_bucket_xqa.cu:57: 1/(1+expf(-g)); vLLM's SiLU-and-mul: g/(1+expf(-g))).
+// Each division and addition is one IEEE fp32 operation.
+QI_DEV float sigmoid_f(float g) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))); }
+QI_DEV float silu_f(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
 
 QI_DEV float warp_sum_butterfly(float v) {
 #pragma unroll

@@ -101,13 +101,20 @@ __global__ void norm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bflo
 #pragma unroll
       for (int j = 0; j < 16; ++j) h[j] = __fadd_rn(h[j], r[j]);
     }
+    // the reference's per-thread order: h0^2, h8^2, h1^2, h9^2, ... h7^2, h15^2
+    // (nvfp4_norm_pack.cu:23-27: each step adds one element of each 8-half)
     ss = __fmul_rn(h[0], h[0]);
+    ss = __fadd_rn(ss, __fmul_rn(h[8], h[8]));
 #pragma unroll
-    for (int j = 1; j < 16; ++j) ss = __fadd_rn(ss, __fmul_rn(h[j], h[j]));
+    for (int j = 1; j < 8; ++j) {
+      ss = __fadd_rn(ss, __fmul_rn(h[j], h[j]));
+      ss = __fadd_rn(ss, __fmul_rn(h[j + 8], h[j + 8]));
+    }
     if (updated) store16_bf16(updated + base, h);
   }
   const float total = block_sum(ss, scratch);
-  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)hidden), eps)));
+  // CUDA's rsqrtf, as the reference calls it (nvfp4_norm_pack.cu:39)
+  const float inv = rsqrtf(__fadd_rn(__fdiv_rn(total, (float)hidden), eps));
   if (!active) return;
   float w[16], y[16];
   load16_bf16(gamma + 16 * t, w);
@@ -124,97 +131,174 @@ __global__ void norm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bflo
   }
 }
 
-// QK-norm + RoPE + gate split + NVFP4 paged append.  One CTA per row, warp w
-// takes heads w, w + 8, ...; lane l owns E2 = D/64 consecutive elements of
-// each rotary half.  The row's position, its cos/sin values and the norm
-// weights are loaded once per row and reused by every head.
-template <int E2>
-__global__ void __launch_bounds__(256) front_kernel(QiFront p) {
-  constexpr int D = E2 * 64, HALF = D / 2;
+// QK-norm + RoPE + gate split + NVFP4 paged append.  One CTA per row.  A head
+// of D values is handled by L = D/16 lanes: lane `sub` of the head owns the 8
+// consecutive elements [8 sub, 8 sub + 8) of each rotary half (16-byte loads
+// and stores), so a warp takes 32/L heads at once and the row's heads are
+// split into warp tasks (Q heads first, then K heads, each K task also
+// appending its V head).
+//
+// The sum of squares follows the reference kernel's tree exactly
+// (nvfp4_attention_front.cu:72-82): pair t = (element t, element t + D/2) is
+// one reference thread with partial x^2 + y^2; 32 consecutive pairs form a
+// reference warp reduced by shfl_down (16, 8, 4, 2, 1), and the warp partials
+// by a second shfl_down tree over lanes padded with zeros.  Pair t = 8 sub + e
+// lives in lane `sub`, element e, so: the 16-step pairs lanes sub and sub ^ 2,
+// the 8-step sub and sub ^ 1, the 4/2/1 steps stay inside the lane, and the
+// warp partials sit in subs 0, 4, 8, 12.  Then rsqrtf as the reference.
+QI_DEV float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+QI_DEV float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+QI_DEV void load8_bf16(const __nv_bfloat16* p, float* out) {
+  const uint4 a = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    out[2 * i] = bf16_lo(w[i]);
+    out[2 * i + 1] = bf16_hi(w[i]);
+  }
+}
+
+QI_DEV void store8_bf16(__nv_bfloat16* p, const float* v) {
+  uint4 a;
+  __nv_bfloat162* pa = reinterpret_cast<__nv_bfloat162*>(&a);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) pa[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = a;
+}
+
+QI_DEV void load8_trig(const void* base, int64_t off, bool is_float, float* out) {
+  if (is_float) {
+    const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(base) + off);
+    const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(base) + off + 4);
+    out[0] = a.x, out[1] = a.y, out[2] = a.z, out[3] = a.w;
+    out[4] = b.x, out[5] = b.y, out[6] = b.z, out[7] = b.w;
+  } else {
+    load8_bf16(static_cast<const __nv_bfloat16*>(base) + off, out);
+  }
+}
+
+// Sum of squares of one head over its L lanes in the reference's tree order.
+template <int L>
+QI_DEV float head_sum_squares(const float* x, const float* y) {
+  float v[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(__fmul_rn(x[e], x[e]), __fmul_rn(y[e], y[e]));
+  if constexpr (L >= 4) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], __shfl_xor_sync(0xffffffffu, v[e], 2));  // pairs t, t+16
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], __shfl_xor_sync(0xffffffffu, v[e], 1));  // t, t+8
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) v[e] = __fadd_rn(v[e], v[e + 4]);
+  v[0] = __fadd_rn(v[0], v[2]);
+  v[1] = __fadd_rn(v[1], v[3]);
+  float p = __fadd_rn(v[0], v[1]);  // this reference warp's partial, valid in subs 0, 4, 8, 12
+  if constexpr (L == 16) {
+    p = __fadd_rn(p, __shfl_xor_sync(0xffffffffu, p, 8));  // warps w, w + 2
+    p = __fadd_rn(p, __shfl_xor_sync(0xffffffffu, p, 4));  // then w, w + 1
+  } else if constexpr (L == 8) {
+    p = __fadd_rn(p, __shfl_xor_sync(0xffffffffu, p, 4));
+  }
+  const int lane = threadIdx.x & 31;
+  return __shfl_sync(0xffffffffu, p, lane & ~(L - 1));  // from the head's sub 0
+}
+
+// NVFP4 of 8 values of one lane; the 16-element group spans lanes sub, sub^1.
+// scale = e4m3(amax / (6 g)), code = e2m1(v * 1/(scale g))
+// (nvfp4_attention_front.cu:45-66).  Returns the 4 code bytes; the scale byte
+// goes to *scale_code.
+QI_DEV uint32_t kv_quant8(const float* v, float g, uint32_t* scale_code) {
+  float amax = 0.0f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[e]));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  const uint32_t code = f_to_e4m3(__fdiv_rn(amax, __fmul_rn(6.0f, g)));
+  const float scale = e4m3_to_f(code);
+  const float inverse = scale > 0.0f ? __fdiv_rn(1.0f, __fmul_rn(scale, g)) : 0.0f;
+  float t[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) t[e] = __fmul_rn(v[e], inverse);
+  *scale_code = code;
+  return f8_to_e2m1x8(t);
+}
+
+template <int D>
+__global__ void __launch_bounds__(512) front_kernel(QiFront p) {
+  constexpr int HALF = D / 2, L = D / 16, HPW = 32 / L;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = lane % L, hsel = lane / L;
   const int64_t row = blockIdx.x;
-  const int d0 = lane * E2;
+  const int d0 = sub * 8;
   const __nv_bfloat16* qkv = static_cast<const __nv_bfloat16*>(p.qkv);
   const int64_t pos = p.pos_long ? static_cast<const int64_t*>(p.positions)[row]
                                  : static_cast<const int32_t*>(p.positions)[row];
-  float cs[E2], sn[E2], wq[2][E2], wk[2][E2];
-  {
-    const __nv_bfloat16* qw = static_cast<const __nv_bfloat16*>(p.q_weight);
-    const __nv_bfloat16* kw = static_cast<const __nv_bfloat16*>(p.k_weight);
+  float cs[8], sn[8], wq[2][8], wk[2][8];
+  load8_trig(p.cos_sin, pos * p.cos_row + d0, p.cos_float, cs);
+  load8_trig(p.cos_sin, pos * p.cos_row + HALF + d0, p.cos_float, sn);
+  load8_bf16(static_cast<const __nv_bfloat16*>(p.q_weight) + d0, wq[0]);
+  load8_bf16(static_cast<const __nv_bfloat16*>(p.q_weight) + HALF + d0, wq[1]);
+  load8_bf16(static_cast<const __nv_bfloat16*>(p.k_weight) + d0, wk[0]);
+  load8_bf16(static_cast<const __nv_bfloat16*>(p.k_weight) + HALF + d0, wk[1]);
 #pragma unroll
-    for (int i = 0; i < E2; ++i) {
-      const int64_t co = pos * p.cos_row + d0 + i;
-      if (p.cos_float) {
-        cs[i] = static_cast<const float*>(p.cos_sin)[co];
-        sn[i] = static_cast<const float*>(p.cos_sin)[co + HALF];
-      } else {
-        cs[i] = __bfloat162float(static_cast<const __nv_bfloat16*>(p.cos_sin)[co]);
-        sn[i] = __bfloat162float(static_cast<const __nv_bfloat16*>(p.cos_sin)[co + HALF]);
-      }
-      wq[0][i] = __fadd_rn(__bfloat162float(qw[d0 + i]), p.weight_offset);
-      wq[1][i] = __fadd_rn(__bfloat162float(qw[HALF + d0 + i]), p.weight_offset);
-      wk[0][i] = __fadd_rn(__bfloat162float(kw[d0 + i]), p.weight_offset);
-      wk[1][i] = __fadd_rn(__bfloat162float(kw[HALF + d0 + i]), p.weight_offset);
-    }
+  for (int e = 0; e < 8; ++e) {
+    wq[0][e] = __fadd_rn(wq[0][e], p.weight_offset);
+    wq[1][e] = __fadd_rn(wq[1][e], p.weight_offset);
+    wk[0][e] = __fadd_rn(wk[0][e], p.weight_offset);
+    wk[1][e] = __fadd_rn(wk[1][e], p.weight_offset);
   }
   int64_t slot = -1;
   if (row < p.slot_rows)
     slot = p.slot_long ? static_cast<const int64_t*>(p.slots)[row] : static_cast<const int32_t*>(p.slots)[row];
-  for (int head = warp; head < p.qheads + p.kvheads; head += 8) {
-    const bool is_k = head >= p.qheads;
-    const int local = is_k ? head - p.qheads : head;
-    if (is_k && slot < 0) break;  // padding token (or past slot_rows): nothing to append
+  const int q_tasks = (p.qheads + HPW - 1) / HPW;
+  const int tasks = q_tasks + (p.kvheads + HPW - 1) / HPW;
+  for (int task = warp; task < tasks; task += blockDim.x >> 5) {  // warp-uniform
+    const bool is_k = task >= q_tasks;
+    const int local = (is_k ? task - q_tasks : task) * HPW + hsel;
+    const bool live = local < (is_k ? p.kvheads : p.qheads);
+    if (is_k && (slot < 0 || row >= p.slot_rows)) continue;  // padding token: nothing to append
     const int64_t base =
         row * p.input_row + (is_k ? (int64_t)p.qheads * 2 * D + (int64_t)local * D : (int64_t)local * 2 * D);
-    float x[E2], y[E2];
+    float x[8], y[8];
+    if (live) {
+      load8_bf16(qkv + base + d0, x);
+      load8_bf16(qkv + base + HALF + d0, y);
+    } else {
 #pragma unroll
-    for (int i = 0; i < E2; ++i) {
-      x[i] = __bfloat162float(qkv[base + d0 + i]);
-      y[i] = __bfloat162float(qkv[base + HALF + d0 + i]);
+      for (int e = 0; e < 8; ++e) x[e] = y[e] = 0.0f;
     }
-    float ss = __fmul_rn(x[0], x[0]);
-    ss = __fadd_rn(ss, __fmul_rn(y[0], y[0]));
-#pragma unroll
-    for (int i = 1; i < E2; ++i) {
-      ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));
-      ss = __fadd_rn(ss, __fmul_rn(y[i], y[i]));
-    }
-    ss = warp_sum_butterfly(ss);
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), p.eps)));
+    const float total = head_sum_squares<L>(x, y);
+    const float inv = rsqrtf(__fadd_rn(__fdiv_rn(total, (float)D), p.eps));  // nvfp4_attention_front.cu:81
     const float* w0 = is_k ? wk[0] : wq[0];
     const float* w1 = is_k ? wk[1] : wq[1];
 #pragma unroll
-    for (int i = 0; i < E2; ++i) {
-      const float a = bf16r(__fmul_rn(__fmul_rn(x[i], inv), w0[i]));
-      const float b = bf16r(__fmul_rn(__fmul_rn(y[i], inv), w1[i]));
-      x[i] = bf16r(__fsub_rn(__fmul_rn(a, cs[i]), __fmul_rn(b, sn[i])));
-      y[i] = bf16r(__fadd_rn(__fmul_rn(b, cs[i]), __fmul_rn(a, sn[i])));
+    for (int e = 0; e < 8; ++e) {
+      const float a = bf16r(__fmul_rn(__fmul_rn(x[e], inv), w0[e]));
+      const float b = bf16r(__fmul_rn(__fmul_rn(y[e], inv), w1[e]));
+      x[e] = bf16r(__fsub_rn(__fmul_rn(a, cs[e]), __fmul_rn(b, sn[e])));
+      y[e] = bf16r(__fadd_rn(__fmul_rn(b, cs[e]), __fmul_rn(a, sn[e])));
     }
     if (!is_k) {
+      if (!live) continue;
       __nv_bfloat16* q = static_cast<__nv_bfloat16*>(p.q) + row * p.q_row + (int64_t)local * D;
-#pragma unroll
-      for (int i = 0; i < E2; ++i) {
-        q[d0 + i] = __float2bfloat16_rn(x[i]);
-        q[HALF + d0 + i] = __float2bfloat16_rn(y[i]);
-      }
+      store8_bf16(q + d0, x);
+      store8_bf16(q + HALF + d0, y);
       if (p.gate) {
         __nv_bfloat16* g = static_cast<__nv_bfloat16*>(p.gate) + row * p.gate_row + (int64_t)local * D;
-#pragma unroll
-        for (int i = 0; i < E2; ++i) {
-          g[d0 + i] = qkv[base + D + d0 + i];
-          g[HALF + d0 + i] = qkv[base + D + HALF + d0 + i];
-        }
+        *reinterpret_cast<uint4*>(g + d0) = *reinterpret_cast<const uint4*>(qkv + base + D + d0);
+        *reinterpret_cast<uint4*>(g + HALF + d0) = *reinterpret_cast<const uint4*>(qkv + base + D + HALF + d0);
       }
       continue;
     }
     if (slot >= (int64_t)p.pages * p.page_size) {
       if (lane == 0) report(p.status, kStatusBadSlot);
-      break;
+      continue;
     }
     const float kg = *p.k_global, vg = *p.v_global;
     if (!(isfinite(kg) && kg > 0.0f && isfinite(vg) && vg > 0.0f)) {
       if (lane == 0) report(p.status, kStatusBadKvScale);
-      break;
+      continue;
     }
     const int64_t page = slot / p.page_size, entry = slot % p.page_size;
     const int64_t data = page * p.data_page + entry * p.data_row + (int64_t)local * p.data_head;
@@ -225,34 +309,18 @@ __global__ void __launch_bounds__(256) front_kernel(QiFront p) {
       uint8_t* codes = static_cast<uint8_t*>(which ? p.v_cache : p.k_cache) + data;
       uint8_t* scales = static_cast<uint8_t*>(which ? p.v_scales : p.k_scales) + sfo;
       const float g = which ? vg : kg;
-      if (which) {
-#pragma unroll
-        for (int i = 0; i < E2; ++i) {
-          x[i] = __bfloat162float(qkv[vbase + d0 + i]);
-          y[i] = __bfloat162float(qkv[vbase + HALF + d0 + i]);
-        }
+      if (which && live) {  // V: the raw projection values (no norm, no rotation)
+        load8_bf16(qkv + vbase + d0, x);
+        load8_bf16(qkv + vbase + HALF + d0, y);
       }
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const float* v = half ? y : x;
-        const int dstart = half * HALF + d0;
-        float amax = 0.0f;
-#pragma unroll
-        for (int i = 0; i < E2; ++i) amax = fmaxf(amax, fabsf(v[i]));
-#pragma unroll
-        for (int d = 1; d < 16 / E2; d <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
-        const uint32_t code = f_to_e4m3(__fdiv_rn(amax, __fmul_rn(6.0f, g)));
-        const float scale = e4m3_to_f(code);
-        const float inverse = scale > 0.0f ? __fdiv_rn(1.0f, __fmul_rn(scale, g)) : 0.0f;
-        if ((dstart & 15) == 0) scales[dstart >> 4] = (uint8_t)code;
-        if constexpr (E2 == 1) {
-          const float mine = __fmul_rn(v[0], inverse);
-          const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
-          if ((lane & 1) == 0) codes[dstart >> 1] = (uint8_t)f2_to_e2m1x2(mine, other);
-        } else {
-#pragma unroll
-          for (int i = 0; i < E2; i += 2)
-            codes[(dstart + i) >> 1] = (uint8_t)f2_to_e2m1x2(__fmul_rn(v[i], inverse), __fmul_rn(v[i + 1], inverse));
+      uint32_t sx, sy;
+      const uint32_t cx = kv_quant8(x, g, &sx), cy = kv_quant8(y, g, &sy);
+      if (live) {
+        *reinterpret_cast<uint32_t*>(codes + (d0 >> 1)) = cx;
+        *reinterpret_cast<uint32_t*>(codes + ((HALF + d0) >> 1)) = cy;
+        if ((sub & 1) == 0) {
+          scales[d0 >> 4] = (uint8_t)sx;
+          scales[(HALF + d0) >> 4] = (uint8_t)sy;
         }
       }
     }
@@ -263,9 +331,12 @@ __global__ void __launch_bounds__(256) front_kernel(QiFront p) {
 // head_stride + c % head_dim: a compact [rows, cols] gate (head_dim = cols),
 // or the gate halves read in place from the QKV projection's per-head
 // [q(D) | gate(D)] blocks (head_dim = D, head_stride = 2D).
+// With static_scale (the reference's form: one per-tensor scale) the row
+// maximum is not taken and scale_out is not written.
 __global__ void gate_fp8_kernel(const __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ gate,
                                 int64_t out_row, int64_t gate_row, int head_dim, int64_t head_stride,
-                                uint8_t* __restrict__ fp8, int64_t fp8_row, float* __restrict__ scale_out, int cols) {
+                                uint8_t* __restrict__ fp8, int64_t fp8_row, float* __restrict__ scale_out, int cols,
+                                const float* __restrict__ static_scale) {
   __shared__ float scratch[33];
   const int64_t row = blockIdx.x;
   const int t = threadIdx.x;
@@ -286,9 +357,14 @@ __global__ void gate_fp8_kernel(const __nv_bfloat16* __restrict__ out, const __n
       amax = fmaxf(amax, fmaxf(fabsf(v0), fabsf(v1)));
     }
   }
-  amax = block_max(amax, scratch);
-  const float scale = fmaxf(__fdiv_rn(amax, 448.0f), 1.17549435e-38f);
-  if (t == 0) scale_out[row] = scale;
+  float scale;
+  if (static_scale) {
+    scale = *static_scale;
+  } else {
+    amax = block_max(amax, scratch);
+    scale = fmaxf(__fdiv_rn(amax, 448.0f), 1.17549435e-38f);
+    if (t == 0) scale_out[row] = scale;
+  }
   if (!active) return;
   uint32_t w[4];
 #pragma unroll
@@ -448,14 +524,14 @@ __global__ void __launch_bounds__(256) kv_dequant_kernel(const uint8_t* __restri
 }
 
 // Element-wise conversion check: E2M1 codes of in[i] (pairs packed as the
-// kernels pack them), E4M3 codes, and fexp / sigmoid of in[i].
+// kernels pack them), E4M3 codes, and expf / sigmoid of in[i].
 __global__ void convert_probe_kernel(const float* __restrict__ in, uint8_t* __restrict__ e2m1_pairs,
                                      uint8_t* __restrict__ e4m3, float* __restrict__ ex, int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const float v = in[i];
   e4m3[i] = (uint8_t)f_to_e4m3(v);
-  ex[2 * i] = fexp(v);
+  ex[2 * i] = expf(v);
   ex[2 * i + 1] = sigmoid_f(v);
   if ((i & 1) == 0 && i + 1 < n) e2m1_pairs[i >> 1] = (uint8_t)f2_to_e2m1x2(v, in[i + 1]);
   if ((i & 7) == 0 && i + 7 < n) {
@@ -550,12 +626,27 @@ int qi_qk_rope_kv_append(const QiFront* p, cudaStream_t stream) {
                            !p->k_scales || !p->v_scales))
     return (int)cudaErrorInvalidValue;
   if (p->slot_rows > p->rows) return (int)cudaErrorInvalidValue;
+  // 16-byte loads / stores of 8 bf16 values (and of 8 fp32 cos/sin values),
+  // 4-byte code stores
+  const int d = p->head_dim;
+  if (!aligned16(p->qkv) || !aligned16(p->q) || (p->gate && !aligned16(p->gate)) || !aligned16(p->cos_sin) ||
+      !aligned16(p->q_weight) || !aligned16(p->k_weight) || p->input_row % 8 || p->q_row % 8 ||
+      (p->gate && p->gate_row % 8) || p->cos_row % (p->cos_float ? 4 : 8))
+    return (int)cudaErrorInvalidValue;
+  if (p->slot_rows > 0 &&
+      ((reinterpret_cast<uintptr_t>(p->k_cache) & 3) || (reinterpret_cast<uintptr_t>(p->v_cache) & 3) ||
+       p->data_page % 4 || p->data_row % 4 || p->data_head % 4))
+    return (int)cudaErrorInvalidValue;
+  if (d != 64 && d != 128 && d != 256) return (int)cudaErrorInvalidValue;
+  const int hpw = 32 / (d / 16);
+  const int tasks = (p->qheads + hpw - 1) / hpw + (p->kvheads + hpw - 1) / hpw;
+  const int rounds = (tasks + 15) / 16;             // at most 16 warps
+  const int warps = (tasks + rounds - 1) / rounds;  // tasks spread evenly over the warps
   const dim3 grid(p->rows);
-  switch (p->head_dim) {
-    case 64: front_kernel<1><<<grid, 256, 0, stream>>>(*p); break;
-    case 128: front_kernel<2><<<grid, 256, 0, stream>>>(*p); break;
-    case 256: front_kernel<4><<<grid, 256, 0, stream>>>(*p); break;
-    default: return (int)cudaErrorInvalidValue;
+  switch (d) {
+    case 64: front_kernel<64><<<grid, warps * 32, 0, stream>>>(*p); break;
+    case 128: front_kernel<128><<<grid, warps * 32, 0, stream>>>(*p); break;
+    default: front_kernel<256><<<grid, warps * 32, 0, stream>>>(*p); break;
   }
   return (int)cudaPeekAtLastError();
 }
@@ -564,9 +655,9 @@ int qi_qk_rope_kv_append_resources(int* out) {
   if (!out) return (int)cudaErrorInvalidValue;
   cudaFuncAttributes a{};
   int occupancy = 0;
-  cudaError_t e = cudaFuncGetAttributes(&a, front_kernel<2>);
+  cudaError_t e = cudaFuncGetAttributes(&a, front_kernel<128>);
   if (e != cudaSuccess) return (int)e;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occupancy, front_kernel<2>, 256, 0);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occupancy, front_kernel<128>, 288, 0);
   if (e != cudaSuccess) return (int)e;
   out[0] = (int)sizeof(QiFront);
   out[1] = a.numRegs;
@@ -646,11 +737,12 @@ int qi_swiglu_nvfp4(const void* gate_up, int64_t gu_row, int rows, int inter, co
   return (int)cudaPeekAtLastError();
 }
 
-int qi_gate_fp8_heads(const void* out, const void* gate, int64_t out_row, int64_t gate_row, int64_t gate_head_stride,
-                      int head_dim, void* fp8, int64_t fp8_row, float* scale, int rows, int cols,
-                      cudaStream_t stream) {
+static int gate_fp8_launch(const void* out, const void* gate, int64_t out_row, int64_t gate_row,
+                           int64_t gate_head_stride, int head_dim, void* fp8, int64_t fp8_row, float* scale,
+                           const float* static_scale, int rows, int cols, cudaStream_t stream) {
   QI_BIND(stream, out);
-  if (rows < 1 || cols < 16 || cols % 16 || cols > 16384 || !out || !gate || !fp8 || !scale || head_dim < 16 ||
+  if (rows < 1 || cols < 16 || cols % 16 || cols > 16384 || !out || !gate || !fp8 || !(scale || static_scale) ||
+      head_dim < 16 ||
       head_dim % 16 || cols % head_dim || gate_head_stride < 0 || gate_head_stride % 8 ||
       (cols > head_dim && gate_head_stride < head_dim))
     return (int)cudaErrorInvalidValue;
@@ -659,8 +751,25 @@ int qi_gate_fp8_heads(const void* out, const void* gate, int64_t out_row, int64_
   const int threads = ((cols / 16) + 31) / 32 * 32;
   gate_fp8_kernel<<<rows, threads, 0, stream>>>(static_cast<const __nv_bfloat16*>(out),
                                                 static_cast<const __nv_bfloat16*>(gate), out_row, gate_row, head_dim,
-                                                gate_head_stride, static_cast<uint8_t*>(fp8), fp8_row, scale, cols);
+                                                gate_head_stride, static_cast<uint8_t*>(fp8), fp8_row, scale, cols,
+                                                static_scale);
   return (int)cudaPeekAtLastError();
+}
+
+int qi_gate_fp8_heads(const void* out, const void* gate, int64_t out_row, int64_t gate_row, int64_t gate_head_stride,
+                      int head_dim, void* fp8, int64_t fp8_row, float* scale, int rows, int cols,
+                      cudaStream_t stream) {
+  if (!scale) return (int)cudaErrorInvalidValue;
+  return gate_fp8_launch(out, gate, out_row, gate_row, gate_head_stride, head_dim, fp8, fp8_row, scale, nullptr, rows,
+                         cols, stream);
+}
+
+int qi_gate_fp8_static(const void* out, const void* gate, int64_t out_row, int64_t gate_row,
+                       int64_t gate_head_stride, int head_dim, void* fp8, int64_t fp8_row, const float* scale,
+                       int rows, int cols, cudaStream_t stream) {
+  if (!scale) return (int)cudaErrorInvalidValue;
+  return gate_fp8_launch(out, gate, out_row, gate_row, gate_head_stride, head_dim, fp8, fp8_row, nullptr, scale, rows,
+                         cols, stream);
 }
 
 int qi_gate_fp8(const void* out, const void* gate, int64_t out_row, int64_t gate_row, void* fp8, int64_t fp8_row,

@@ -1,9 +1,10 @@
 """Regenerate the golden fixtures recorded from the reference project itself.
 
-Needs the reference checkout (read-only) at $QVPP_REFERENCE (the default
-is the REF path below) and, for the wire headers, the reference C++ sources
-compiled by ``oracle/build_ref.py``.  The committed JSON fixtures are what the
-tests read; this script is only how they were made.
+Needs the reference checkout (read-only) at $QVPP_REFERENCE (default: a
+checkout named ``reference`` beside this repository) and, for the wire
+headers, the reference C++ sources compiled by ``oracle/build_ref.py``.
+The committed JSON fixtures are what the tests read; this script is only
+how they were made.
 
     python tests/golden/make_golden.py
 """
@@ -17,7 +18,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(os.environ.get("QVPP_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("QVPP_REFERENCE", str(REPO.parent / "reference")))
 
 
 def _load(name, path):

@@ -31,7 +31,7 @@ def _bf16(shape, seed, std=1.0, mean=0.0):
 
 
 def test_conversion_builtins_match_format_definitions(K):
-    """E2M1 / E4M3 rounding, nibble order and fexp/sigmoid of the device
+    """E2M1 / E4M3 rounding, nibble order and expf / sigmoid of the device
     helpers against the CPU restatement, including ties and saturation."""
     from qwen_infra_b200 import _native as N
     import ctypes as ct
@@ -60,15 +60,15 @@ def test_conversion_builtins_match_format_definitions(K):
     assert np.array_equal(e2.cpu().numpy()[n // 2:], packed)
     assert np.array_equal(e4.cpu().numpy(), F.e4m3_encode(grid))
     exv = ex.cpu().numpy().reshape(n, 2)
-    assert np.array_equal(exv[:, 0], P.fexp(grid))
+    # the product library's expf is CUDA's (same values as the oracle's helper
+    # built with the reference's flags), and its sigmoid the reference's
+    assert np.array_equal(exv[:, 0], P.MATH.exp(grid))
     assert np.array_equal(exv[:, 1], P.sigmoid_f(grid))
-    # accuracy of the published exp method against float64
+    # CUDA's expf: within 2 ulp of exp (the documented maximum ulp error)
     ref = np.exp(np.clip(grid, -80, 80).astype(np.float64))
     mask = np.abs(grid) < 80
-    rel = np.abs(exv[mask, 0] - ref[mask]) / ref[mask]
-    # polynomial and rounding (< 1e-6) plus the rounding of t = x*log2(e),
-    # which is worth ln2 * |t| * 2^-24 ~ 6e-8 |x| relative
-    assert np.all(rel < 1e-6 + 6e-8 * np.abs(grid[mask]))
+    ulp = np.spacing(ref[mask].astype(np.float32)).astype(np.float64)
+    assert np.all(np.abs(exv[mask, 0] - ref[mask]) <= 2 * ulp)
 
 
 @pytest.mark.parametrize("rows,h,with_res", [(1, 1024, True), (17, 1024, False), (129, 1024, True),

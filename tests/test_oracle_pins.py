@@ -6,6 +6,7 @@ import json
 from pathlib import Path
 
 import numpy as np
+import pytest
 import torch
 
 from oracle import formats as F
@@ -76,12 +77,16 @@ def test_nvfp4_quant_dequant_error_bound():
     assert np.all(np.abs(back - w).reshape(64, 16, 16).max(-1) <= blk * (1 / 6 + 1 / 16) + 1e-6)
 
 
-def test_fexp_accuracy_and_sigmoid_range():
+def test_host_math_and_sigmoid_range():
     x = np.linspace(-80, 80, 100001, dtype=np.float32)
-    rel = np.abs(P.fexp(x).astype(np.float64) - np.exp(x.astype(np.float64))) / np.exp(x.astype(np.float64))
-    assert np.all(rel < 1e-6 + 6e-8 * np.abs(x))
+    assert np.array_equal(P.HostMath().exp(x), np.exp(x.astype(np.float64)).astype(np.float32))
     s = P.sigmoid_f(np.array([-1000, -10, 0, 10, 1000], np.float32))
     assert s[0] == 0 and s[2] == 0.5 and s[4] == 1
+    rec = P.RecordedMath(rsqrt={int(np.float32(4.0).view(np.uint32)): int(np.float32(0.25).view(np.uint32))})
+    assert rec.rsqrt(np.array([4.0, 16.0], np.float32)).tolist() == [0.25, 0.25]
+    with P.use_math(rec):
+        assert P.MATH is rec
+    assert isinstance(P.MATH, P.HostMath) and P.MATH is not rec
 
 
 def test_gate_fp8_per_token_scale_properties():
@@ -108,3 +113,35 @@ def test_lm_head_argmax_oracle_ties_and_nan():
     w2 = np.full((3, 8), -1.0, dtype=np.float32)
     w2[2] = -0.5  # all negative: the largest (least negative) wins
     assert P.lm_head_argmax(h, w2)[1].tolist() == [2, 2]
+
+
+def _producer_golden():
+    import importlib.util
+
+    path = Path(__file__).resolve().parent / "golden" / "producers_ref.json"
+    if not path.exists():
+        pytest.skip("producers_ref.json not recorded yet (tests/golden/make_producer_golden.py on a B200)")
+    spec = importlib.util.spec_from_file_location("make_producer_golden", path.parent / "make_producer_golden.py")
+    gen = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(gen)
+    return gen, json.loads(path.read_text())
+
+
+def test_oracle_reproduces_reference_producer_bytes():
+    """The reference's norm-pack, attention front (D 256, page 32) and FP8 gate
+    epilogue, run on a B200 from its own sources, recorded as output hashes:
+    the CPU oracle rebuilds every output byte from the seeded inputs, given
+    CUDA's rsqrtf / expf values where they differ from the correctly rounded
+    ones (recorded beside the hashes)."""
+    gen, golden = _producer_golden()
+    checked = 0
+    for kind, cases in golden["cases"].items():
+        for case in cases:
+            math = P.RecordedMath(rsqrt={int(k): v for k, v in case["rsqrt_differs"].items()},
+                                  exp={int(k): v for k, v in case["exp_differs"].items()})
+            with P.use_math(math):
+                outs = gen.oracle_outputs(kind, case["spec"])
+            for name, digest in case["sha256"].items():
+                assert gen.sha(np.asarray(outs[name])) == digest, (kind, case["spec"], name)
+                checked += 1
+    assert checked >= 10
