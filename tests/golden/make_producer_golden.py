@@ -121,6 +121,9 @@ def reference_outputs(kind, spec):
     """Outputs of the reference kernels (GPU) for one case."""
     import torch
 
+    import __graft_entry__
+
+    __graft_entry__.load_package()
     sys.path.insert(0, str(REPO / "tests"))
     import test_ref_pin_gpu as T
     from oracle import cuda_math
