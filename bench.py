@@ -24,6 +24,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -67,9 +68,13 @@ def parse():
                    help="one GPU: run the two virtual stages on two CUDA streams (auto: on for N=1)")
     p.add_argument("--kv-shadow", choices=("auto", "on", "off"), default="auto",
                    help="keep each request's f16 K/V^T across its chunks (dequantise new tokens only)")
-    p.add_argument("--workload", choices=("prefill", "decode"), default="prefill",
+    p.add_argument("--workload", choices=("prefill", "decode", "producers"), default="prefill",
                    help="prefill: the folded-VPP bank (default); decode: the bucket decode attention over the "
-                        "paged NVFP4 cache (one query token per request, 1 GPU)")
+                        "paged NVFP4 cache (one query token per request, 1 GPU); producers: the fused-operator "
+                        "microbench of config 2 (norm-pack, QK-norm/RoPE/KV append, gate->FP8, 1 GPU)")
+    p.add_argument("--producer-rows", type=int, default=2048)
+    p.add_argument("--clocks-dir", default=None,
+                   help="directory for the nvidia-smi clock samples (default: a fresh temporary directory)")
     p.add_argument("--decode-batch", type=int, default=32)
     p.add_argument("--decode-context", type=int, default=32768)
     p.add_argument("--decode-mode", choices=("auto", "native", "persistent", "aligned"), default="persistent",
@@ -274,7 +279,8 @@ def run_ours(args):
     runner.model.check_status()
 
     # --- timed: inputs resident in HBM -----------------------------------
-    sampler = ClockSampler(REPO / "gpurun_out" / f"clocks_rank{rank}.csv") if rank == 0 else None
+    sampler = ClockSampler(Path(args.clocks_dir or tempfile.mkdtemp(prefix="qi_clocks_")) / f"clocks_rank{rank}.csv") \
+        if rank == 0 else None
     counter = K.LaunchProfile(timing=False)  # counts this library's launches only
     K.PROFILE = counter
     barrier()
@@ -507,7 +513,7 @@ def run_decode(args):
     steps = max(args.steps, 20)
     counter = K.LaunchProfile(timing=False)
     K.PROFILE = counter
-    sampler = ClockSampler(REPO / "gpurun_out" / "clocks_decode.csv")
+    sampler = ClockSampler(Path(args.clocks_dir or tempfile.mkdtemp(prefix="qi_clocks_")) / "clocks_decode.csv")
     sampler.start()
     times = []
     for _ in range(steps):
@@ -568,10 +574,177 @@ def run_decode(args):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# Producers workload: the fused-operator microbench
+# ---------------------------------------------------------------------------
+PRODUCERS_METRIC = ("fused producers at 2048 rows (norm->NVFP4, QK-norm/RoPE/NVFP4 KV append, gate->FP8): "
+                    "HBM GB/s")
+
+
+def producer_inputs(rows, device, seed=2):
+    """Config 2: hidden 5120, 64 Q / 8 KV heads of 128, page 16; bf16 residual
+    and hidden ~N(0,1), norm weights ~1+N(0,0.05), positions 0..rows-1."""
+    import torch
+
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    h, qh, kvh, d = 5120, 64, 8, 128
+
+    def rnd(*shape, std=1.0, mean=0.0):
+        return (torch.randn(*shape, generator=g) * std + mean).to(torch.bfloat16).to(device)
+
+    return dict(x=rnd(rows, h), r=rnd(rows, h), w=rnd(h, std=0.05, mean=1.0),
+                qkv=rnd(rows, (2 * qh + 2 * kvh) * d), qw=rnd(d, std=0.05, mean=1.0), kw=rnd(d, std=0.05, mean=1.0),
+                attn=rnd(rows, qh * d), pos=torch.arange(rows, dtype=torch.int32, device=device), h=h, qh=qh,
+                kvh=kvh, d=d)
+
+
+def producer_bytes(rows, h=5120, qh=64, kvh=8, d=128):
+    """Algorithmic bytes per launch of each producer (per row: norm 33,600;
+    front 38,528 with the gate read in place; gate 40,964)."""
+    return dict(norm_pack=rows * (2 * 2 * h + 2 * h + h // 2 + h // 16),
+                qk_rope_kv_append=rows * ((qh + 2 * kvh) * d * 2 + d * 4 + qh * d * 2 + kvh * (d + d // 8)),
+                gate_fp8=rows * (qh * d * 5 + 4))
+
+
+def producers_cpu_sample(threads, rows=64):
+    """The oracle's three producers on ``rows`` rows of config 2 (bounded sample)."""
+    import numpy as np
+    import torch
+    from oracle import model as OM
+    from oracle import producers as P
+
+    torch.set_num_threads(threads)
+    a = producer_inputs(rows, "cpu")
+    f = lambda t: t.float().numpy()
+    kv = OM.KVCache(OM.Shape(1, 5120, 64, 8, 128, 17408, page_size=16), (rows + 15) // 16)
+    cs = OM.rope_table(rows, 128, 1e6)
+    t0 = time.perf_counter()
+    P.norm_pack(f(a["x"]), f(a["r"]), f(a["w"]), 84.0)
+    P.qk_rope_append(f(a["qkv"]), np.arange(rows), f(a["qw"]), f(a["kw"]), cs, np.arange(rows), 16 / 2688,
+                     8 / 2688, kv.k, kv.v, kv.ks, kv.vs, qheads=64, kvheads=8, head_dim=128, page_size=16)
+    gate = f(a["qkv"])[:, : 2 * 64 * 128].reshape(rows, 64, 2, 128)[:, :, 1].reshape(rows, -1)
+    P.gate_fp8(f(a["attn"]), gate)
+    dt = time.perf_counter() - t0
+    return dict(value=sum(producer_bytes(rows).values()) / dt / 1e9, unit="GB/s", cores=threads, kind="port",
+                sample=f"oracle norm-pack + front + gate on {rows} rows of config 2 ({dt:.1f} s)")
+
+
+def run_producers(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    rows = args.producer_rows
+    nbytes = producer_bytes(rows)
+    config = dict(workload=f"config 2 fused producers, {rows} rows, hidden 5120, 64/8 heads of 128, page 16",
+                  rows=rows, l2="L2 flushed (256 MiB write) before every timed launch")
+    if args.impl == "reference":
+        cpu = producers_cpu_sample(threads, rows=min(rows, 2048))
+        total = sum(nbytes.values())
+        line = dict(metric=PRODUCERS_METRIC, value=cpu["value"], unit="GB/s", n_gpus=1, steps=args.steps,
+                    warmup=args.warmup, ms_per_step=total / (cpu["value"] * 1e9) * 1e3, higher_is_better=True,
+                    scaling="weak", vs_baseline=None, dtype="f32", data="synthetic", impl="reference",
+                    config=config, cpu_baseline=cpu,
+                    e2e=dict(value=cpu["value"], unit="GB/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+        print(json.dumps(line), flush=True)
+        return 0
+    import torch
+
+    __graft_entry__.load_package()
+    from qwen_infra_b200 import kernels as K
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    a = producer_inputs(rows, dev)
+    from oracle import model as OM  # the RoPE table only (cos/sin of positions 0..rows-1)
+
+    cs = torch.from_numpy(OM.rope_table(rows, 128, 1e6)).to(dev)
+    kv = K.PagedKV((rows + 15) // 16, 16, 8, 128, dev)
+    slots = a["pos"].clone()
+    gs = torch.tensor([84.0], device=dev)
+    kg, vg = torch.tensor([16 / 2688], device=dev), torch.tensor([8 / 2688], device=dev)
+    q = torch.empty((rows, 64 * 128), dtype=torch.bfloat16, device=dev)
+    gate_view = a["qkv"][:, 128:]
+    ops = dict(
+        norm_pack=lambda: K.norm_pack(a["x"], a["r"], a["w"], gs),
+        qk_rope_kv_append=lambda: K.qk_rope_kv_append(a["qkv"], a["pos"], a["qw"], a["kw"], cs, slots, kv, kg, vg,
+                                                      qheads=64, kvheads=8, head_dim=128, q=q, want_gate=False),
+        gate_fp8=lambda: K.gate_fp8(a["attn"], gate_view, head_dim=128, head_stride=256),
+    )
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(3, args.warmup)):
+        for fn in ops.values():
+            fn()
+    torch.cuda.synchronize()
+    steps = max(args.steps, 20)
+    counter = K.LaunchProfile(timing=False)
+    K.PROFILE = counter
+    sampler = ClockSampler(Path(args.clocks_dir or tempfile.mkdtemp(prefix="qi_clocks_")) / "clocks_producers.csv")
+    sampler.start()
+    times = {name: [] for name in ops}
+    for _ in range(steps):
+        for name, fn in ops.items():
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            times[name].append(e0.elapsed_time(e1))
+    clocks = sampler.stop()
+    K.PROFILE = None
+    peaks, peak_kind = load_peaks()
+    kernels = {}
+    for name in ops:
+        ms = statistics.median(times[name])
+        ach = nbytes[name] / (ms / 1e3) / 1e9
+        kernels[name] = dict(avg_launch_ms=ms, achieved=ach, unit="GB/s", bytes_per_launch=nbytes[name],
+                             frac=ach / peaks["hbm_gbs"])
+    total_ms = sum(k["avg_launch_ms"] for k in kernels.values())
+    value = sum(nbytes.values()) / (total_ms / 1e3) / 1e9
+    dom = max(kernels, key=lambda n: kernels[n]["avg_launch_ms"])
+    # e2e: inputs from pinned host memory, the three producers, outputs read back
+    host_in = {k: a[k].cpu().pin_memory() for k in ("x", "r", "qkv", "attn")}
+    out_host = dict(q=torch.empty(q.shape, dtype=q.dtype).pin_memory())
+    et = []
+    for _ in range(steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for k, t in host_in.items():
+            a[k].copy_(t, non_blocking=True)
+        qn, sfn, upd = ops["norm_pack"]()
+        ops["qk_rope_kv_append"]()
+        fp8, scl = ops["gate_fp8"]()
+        out_host["q"].copy_(q, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        et.append(e0.elapsed_time(e1))
+    ems = statistics.median(et)
+    h2d = sum(t.numel() * t.element_size() for t in host_in.values())
+    cpu = producers_cpu_sample(threads, rows=512) if not args.no_cpu_baseline else None
+    line = dict(
+        metric=PRODUCERS_METRIC, value=value, unit="GB/s", n_gpus=1, steps=steps, warmup=max(3, args.warmup),
+        ms_per_step=total_ms, higher_is_better=True, scaling="weak", vs_baseline=None,
+        dtype="bf16 in, fp32 math, NVFP4 / E4M3 out", data="synthetic (config 2 seeded inputs)", config=config,
+        kernels=kernels,
+        roofline=dict(kernel=dom, bound="hbm", achieved=kernels[dom]["achieved"], peak=peaks["hbm_gbs"],
+                      unit="GB/s", frac=kernels[dom]["achieved"] / peaks["hbm_gbs"],
+                      peak_source=f"hbm_gbs ({peak_kind})", traffic=None),
+        gpu_launches=counter.launches, clocks=clocks,
+        e2e=dict(value=sum(nbytes.values()) / (ems / 1e3) / 1e9, unit="GB/s", ms_per_step=ems,
+                 h2d_bytes_per_step=h2d, d2h_bytes_per_step=q.numel() * 2),
+        cpu_baseline=cpu)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.workload == "decode":
         return run_decode(args)
+    if args.workload == "producers":
+        return run_producers(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
