@@ -637,7 +637,7 @@ def run_producers(args):
     rows = args.producer_rows
     nbytes = producer_bytes(rows)
     config = dict(workload=f"config 2 fused producers, {rows} rows, hidden 5120, 64/8 heads of 128, page 16",
-                  rows=rows, l2="L2 flushed (256 MiB write) before every timed launch")
+                  rows=rows, l2="L2 flushed before every timed launch (256 MiB written, then 256 MiB read)")
     if args.impl == "reference":
         cpu = producers_cpu_sample(threads, rows=min(rows, 2048))
         total = sum(nbytes.values())
@@ -671,7 +671,15 @@ def run_producers(args):
                                                       qheads=64, kvheads=8, head_dim=128, q=q, want_gate=False),
         gate_fp8=lambda: K.gate_fp8(a["attn"], gate_view, head_dim=128, head_stride=256),
     )
+    # L2 flush: write 256 MiB, then read another 256 MiB so that the lines
+    # left in L2 are clean (no write-backs land inside the timed launch)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush_read = torch.zeros(64 << 20, dtype=torch.float32, device=dev)
+
+    def flush_l2():
+        flush.zero_()
+        flush_read.sum()
+
     stream = torch.cuda.current_stream(dev)
     for _ in range(max(3, args.warmup)):
         for fn in ops.values():
@@ -685,7 +693,7 @@ def run_producers(args):
     times = {name: [] for name in ops}
     for _ in range(steps):
         for name, fn in ops.items():
-            flush.zero_()
+            flush_l2()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             fn()

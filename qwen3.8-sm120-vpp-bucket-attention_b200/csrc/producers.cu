@@ -224,104 +224,103 @@ QI_DEV uint32_t kv_quant8(const float* v, float g, uint32_t* scale_code) {
   return f8_to_e2m1x8(t);
 }
 
+// One warp per task: a task is 32/L heads of one kind (Q heads, or K heads
+// with their V heads), so a row has ceil(Hq/HPW) + ceil(Hkv/HPW) tasks and
+// blockIdx.y picks a group of `warpsPerCta` of them.  Every load a warp needs
+// (its heads' values, the V values of a K task, cos/sin and its norm weight)
+// is issued before any arithmetic, so each warp has all its bytes in flight
+// at once; only the weights of the task's own kind are held.
 template <int D>
-__global__ void __launch_bounds__(512) front_kernel(QiFront p) {
+__global__ void __launch_bounds__(256) front_kernel(QiFront p) {
   constexpr int HALF = D / 2, L = D / 16, HPW = 32 / L;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31;
   const int sub = lane % L, hsel = lane / L;
   const int64_t row = blockIdx.x;
   const int d0 = sub * 8;
-  const __nv_bfloat16* qkv = static_cast<const __nv_bfloat16*>(p.qkv);
-  const int64_t pos = p.pos_long ? static_cast<const int64_t*>(p.positions)[row]
-                                 : static_cast<const int32_t*>(p.positions)[row];
-  float cs[8], sn[8], wq[2][8], wk[2][8];
-  load8_trig(p.cos_sin, pos * p.cos_row + d0, p.cos_float, cs);
-  load8_trig(p.cos_sin, pos * p.cos_row + HALF + d0, p.cos_float, sn);
-  load8_bf16(static_cast<const __nv_bfloat16*>(p.q_weight) + d0, wq[0]);
-  load8_bf16(static_cast<const __nv_bfloat16*>(p.q_weight) + HALF + d0, wq[1]);
-  load8_bf16(static_cast<const __nv_bfloat16*>(p.k_weight) + d0, wk[0]);
-  load8_bf16(static_cast<const __nv_bfloat16*>(p.k_weight) + HALF + d0, wk[1]);
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    wq[0][e] = __fadd_rn(wq[0][e], p.weight_offset);
-    wq[1][e] = __fadd_rn(wq[1][e], p.weight_offset);
-    wk[0][e] = __fadd_rn(wk[0][e], p.weight_offset);
-    wk[1][e] = __fadd_rn(wk[1][e], p.weight_offset);
-  }
-  int64_t slot = -1;
-  if (row < p.slot_rows)
-    slot = p.slot_long ? static_cast<const int64_t*>(p.slots)[row] : static_cast<const int32_t*>(p.slots)[row];
   const int q_tasks = (p.qheads + HPW - 1) / HPW;
   const int tasks = q_tasks + (p.kvheads + HPW - 1) / HPW;
-  for (int task = warp; task < tasks; task += blockDim.x >> 5) {  // warp-uniform
-    const bool is_k = task >= q_tasks;
-    const int local = (is_k ? task - q_tasks : task) * HPW + hsel;
-    const bool live = local < (is_k ? p.kvheads : p.qheads);
-    if (is_k && (slot < 0 || row >= p.slot_rows)) continue;  // padding token: nothing to append
-    const int64_t base =
-        row * p.input_row + (is_k ? (int64_t)p.qheads * 2 * D + (int64_t)local * D : (int64_t)local * 2 * D);
-    float x[8], y[8];
+  const int task = blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (task >= tasks) return;  // whole warp
+  const bool is_k = task >= q_tasks;
+  int64_t slot = -1;
+  if (is_k) {
+    if (row >= p.slot_rows) return;  // nothing to append for this row
+    slot = p.slot_long ? static_cast<const int64_t*>(p.slots)[row] : static_cast<const int32_t*>(p.slots)[row];
+    if (slot < 0) return;  // padding token
+  }
+  const int local = (is_k ? task - q_tasks : task) * HPW + hsel;
+  const bool live = local < (is_k ? p.kvheads : p.qheads);
+  const __nv_bfloat16* qkv = static_cast<const __nv_bfloat16*>(p.qkv);
+  const int64_t base =
+      row * p.input_row + (is_k ? (int64_t)p.qheads * 2 * D + (int64_t)local * D : (int64_t)local * 2 * D);
+  const int64_t vbase = row * p.input_row + (int64_t)p.qheads * 2 * D + (int64_t)p.kvheads * D + (int64_t)local * D;
+  float x[8], y[8], vx[8], vy[8];
+  if (live) {
+    load8_bf16(qkv + base + d0, x);
+    load8_bf16(qkv + base + HALF + d0, y);
+    if (is_k) {
+      load8_bf16(qkv + vbase + d0, vx);
+      load8_bf16(qkv + vbase + HALF + d0, vy);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] = y[e] = vx[e] = vy[e] = 0.0f;
+  }
+  const int64_t pos = p.pos_long ? static_cast<const int64_t*>(p.positions)[row]
+                                 : static_cast<const int32_t*>(p.positions)[row];
+  float cs[8], sn[8], w0[8], w1[8];
+  const __nv_bfloat16* wsrc = static_cast<const __nv_bfloat16*>(is_k ? p.k_weight : p.q_weight);
+  load8_bf16(wsrc + d0, w0);
+  load8_bf16(wsrc + HALF + d0, w1);
+  load8_trig(p.cos_sin, pos * p.cos_row + d0, p.cos_float, cs);
+  load8_trig(p.cos_sin, pos * p.cos_row + HALF + d0, p.cos_float, sn);
+  const float total = head_sum_squares<L>(x, y);
+  const float inv = rsqrtf(__fadd_rn(__fdiv_rn(total, (float)D), p.eps));  // nvfp4_attention_front.cu:81
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float a = bf16r(__fmul_rn(__fmul_rn(x[e], inv), __fadd_rn(w0[e], p.weight_offset)));
+    const float b = bf16r(__fmul_rn(__fmul_rn(y[e], inv), __fadd_rn(w1[e], p.weight_offset)));
+    x[e] = bf16r(__fsub_rn(__fmul_rn(a, cs[e]), __fmul_rn(b, sn[e])));
+    y[e] = bf16r(__fadd_rn(__fmul_rn(b, cs[e]), __fmul_rn(a, sn[e])));
+  }
+  if (!is_k) {
+    if (!live) return;
+    __nv_bfloat16* q = static_cast<__nv_bfloat16*>(p.q) + row * p.q_row + (int64_t)local * D;
+    store8_bf16(q + d0, x);
+    store8_bf16(q + HALF + d0, y);
+    if (p.gate) {
+      __nv_bfloat16* g = static_cast<__nv_bfloat16*>(p.gate) + row * p.gate_row + (int64_t)local * D;
+      *reinterpret_cast<uint4*>(g + d0) = *reinterpret_cast<const uint4*>(qkv + base + D + d0);
+      *reinterpret_cast<uint4*>(g + HALF + d0) = *reinterpret_cast<const uint4*>(qkv + base + D + HALF + d0);
+    }
+    return;
+  }
+  if (slot >= (int64_t)p.pages * p.page_size) {
+    if (lane == 0) report(p.status, kStatusBadSlot);
+    return;
+  }
+  const float kg = *p.k_global, vg = *p.v_global;
+  if (!(isfinite(kg) && kg > 0.0f && isfinite(vg) && vg > 0.0f)) {
+    if (lane == 0) report(p.status, kStatusBadKvScale);
+    return;
+  }
+  const int64_t page = slot / p.page_size, entry = slot % p.page_size;
+  const int64_t data = page * p.data_page + entry * p.data_row + (int64_t)local * p.data_head;
+  const int64_t sfo = page * p.sf_page + entry * p.sf_row + (int64_t)local * p.sf_head;
+#pragma unroll
+  for (int which = 0; which < 2; ++which) {
+    uint8_t* codes = static_cast<uint8_t*>(which ? p.v_cache : p.k_cache) + data;
+    uint8_t* scales = static_cast<uint8_t*>(which ? p.v_scales : p.k_scales) + sfo;
+    uint32_t sx, sy;
+    // K: the normed, rotated values; V: the raw projection values
+    const uint32_t cx = kv_quant8(which ? vx : x, which ? vg : kg, &sx);
+    const uint32_t cy = kv_quant8(which ? vy : y, which ? vg : kg, &sy);
     if (live) {
-      load8_bf16(qkv + base + d0, x);
-      load8_bf16(qkv + base + HALF + d0, y);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) x[e] = y[e] = 0.0f;
-    }
-    const float total = head_sum_squares<L>(x, y);
-    const float inv = rsqrtf(__fadd_rn(__fdiv_rn(total, (float)D), p.eps));  // nvfp4_attention_front.cu:81
-    const float* w0 = is_k ? wk[0] : wq[0];
-    const float* w1 = is_k ? wk[1] : wq[1];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float a = bf16r(__fmul_rn(__fmul_rn(x[e], inv), w0[e]));
-      const float b = bf16r(__fmul_rn(__fmul_rn(y[e], inv), w1[e]));
-      x[e] = bf16r(__fsub_rn(__fmul_rn(a, cs[e]), __fmul_rn(b, sn[e])));
-      y[e] = bf16r(__fadd_rn(__fmul_rn(b, cs[e]), __fmul_rn(a, sn[e])));
-    }
-    if (!is_k) {
-      if (!live) continue;
-      __nv_bfloat16* q = static_cast<__nv_bfloat16*>(p.q) + row * p.q_row + (int64_t)local * D;
-      store8_bf16(q + d0, x);
-      store8_bf16(q + HALF + d0, y);
-      if (p.gate) {
-        __nv_bfloat16* g = static_cast<__nv_bfloat16*>(p.gate) + row * p.gate_row + (int64_t)local * D;
-        *reinterpret_cast<uint4*>(g + d0) = *reinterpret_cast<const uint4*>(qkv + base + D + d0);
-        *reinterpret_cast<uint4*>(g + HALF + d0) = *reinterpret_cast<const uint4*>(qkv + base + D + HALF + d0);
-      }
-      continue;
-    }
-    if (slot >= (int64_t)p.pages * p.page_size) {
-      if (lane == 0) report(p.status, kStatusBadSlot);
-      continue;
-    }
-    const float kg = *p.k_global, vg = *p.v_global;
-    if (!(isfinite(kg) && kg > 0.0f && isfinite(vg) && vg > 0.0f)) {
-      if (lane == 0) report(p.status, kStatusBadKvScale);
-      continue;
-    }
-    const int64_t page = slot / p.page_size, entry = slot % p.page_size;
-    const int64_t data = page * p.data_page + entry * p.data_row + (int64_t)local * p.data_head;
-    const int64_t sfo = page * p.sf_page + entry * p.sf_row + (int64_t)local * p.sf_head;
-    const int64_t vbase = row * p.input_row + (int64_t)p.qheads * 2 * D + (int64_t)p.kvheads * D + (int64_t)local * D;
-#pragma unroll
-    for (int which = 0; which < 2; ++which) {
-      uint8_t* codes = static_cast<uint8_t*>(which ? p.v_cache : p.k_cache) + data;
-      uint8_t* scales = static_cast<uint8_t*>(which ? p.v_scales : p.k_scales) + sfo;
-      const float g = which ? vg : kg;
-      if (which && live) {  // V: the raw projection values (no norm, no rotation)
-        load8_bf16(qkv + vbase + d0, x);
-        load8_bf16(qkv + vbase + HALF + d0, y);
-      }
-      uint32_t sx, sy;
-      const uint32_t cx = kv_quant8(x, g, &sx), cy = kv_quant8(y, g, &sy);
-      if (live) {
-        *reinterpret_cast<uint32_t*>(codes + (d0 >> 1)) = cx;
-        *reinterpret_cast<uint32_t*>(codes + ((HALF + d0) >> 1)) = cy;
-        if ((sub & 1) == 0) {
-          scales[d0 >> 4] = (uint8_t)sx;
-          scales[(HALF + d0) >> 4] = (uint8_t)sy;
-        }
+      *reinterpret_cast<uint32_t*>(codes + (d0 >> 1)) = cx;
+      *reinterpret_cast<uint32_t*>(codes + ((HALF + d0) >> 1)) = cy;
+      if ((sub & 1) == 0) {
+        scales[d0 >> 4] = (uint8_t)sx;
+        scales[(HALF + d0) >> 4] = (uint8_t)sy;
       }
     }
   }
@@ -640,9 +639,10 @@ int qi_qk_rope_kv_append(const QiFront* p, cudaStream_t stream) {
   if (d != 64 && d != 128 && d != 256) return (int)cudaErrorInvalidValue;
   const int hpw = 32 / (d / 16);
   const int tasks = (p->qheads + hpw - 1) / hpw + (p->kvheads + hpw - 1) / hpw;
-  const int rounds = (tasks + 15) / 16;             // at most 16 warps
-  const int warps = (tasks + rounds - 1) / rounds;  // tasks spread evenly over the warps
-  const dim3 grid(p->rows);
+  // one warp per task; the row's tasks split evenly over 1..8-warp CTAs
+  const int groups = (tasks + 7) / 8;
+  const int warps = (tasks + groups - 1) / groups;
+  const dim3 grid(p->rows, groups);
   switch (d) {
     case 64: front_kernel<64><<<grid, warps * 32, 0, stream>>>(*p); break;
     case 128: front_kernel<128><<<grid, warps * 32, 0, stream>>>(*p); break;
@@ -657,7 +657,7 @@ int qi_qk_rope_kv_append_resources(int* out) {
   int occupancy = 0;
   cudaError_t e = cudaFuncGetAttributes(&a, front_kernel<128>);
   if (e != cudaSuccess) return (int)e;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occupancy, front_kernel<128>, 288, 0);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occupancy, front_kernel<128>, 192, 0);
   if (e != cudaSuccess) return (int)e;
   out[0] = (int)sizeof(QiFront);
   out[1] = a.numRegs;
