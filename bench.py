@@ -57,6 +57,8 @@ def parse():
     p.add_argument("--prompt-tokens", type=int, default=32768)
     p.add_argument("--chunk-size", type=int, default=2048)
     p.add_argument("--transport", choices=("p2p", "nccl"), default="p2p")
+    p.add_argument("--resource-layout", choices=("rank", "edge"), default=None,
+                   help="boundary slots: rank-shared 2+3 (p2p default) or 7 per edge endpoint (nccl default)")
     p.add_argument("--profile", choices=("vpp", "cpp"), default="vpp",
                    help="vpp: 2N virtual stages folded onto N GPUs; cpp: the conventional N-stage pipeline "
                         "(the comparison arm)")
@@ -251,7 +253,7 @@ def run_ours(args):
         from qwen_infra_b200.vpp.stages import StageBoundaries
 
         transport = StageBoundaries(rank, world, dev, args.chunk_size, shape.hidden, backend=args.transport,
-                                    profile=args.profile)
+                                    profile=args.profile, resource_layout=args.resource_layout)
     request_tokens = [args.prompt_tokens] * args.requests
     runner = FoldedRank(shape, rank, world, dev, request_tokens, args.chunk_size, transport=transport,
                         profile=args.profile, kv_shadow={"auto": None, "on": True, "off": False}[args.kv_shadow],

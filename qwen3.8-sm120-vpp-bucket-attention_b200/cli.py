@@ -65,12 +65,15 @@ class PrefillConfig:
 
 
 def _records(outputs, requests, tokens):
+    import torch
+
     recs = []
     for r in range(requests):
         v = outputs[r]
+        raw = v.detach().to("cpu").contiguous().view(-1).view(torch.uint8).numpy().tobytes()  # any dtype
         recs.append(dict(request_id=str(r), text="", token_ids=[int(tokens[r])], finished=True,
-                         final_hidden_norm=float(v.norm()),
-                         final_hidden_sha256=hashlib.sha256(v.to("cpu").numpy().tobytes()).hexdigest()[:16]))
+                         final_hidden_norm=float(v.float().norm()),
+                         final_hidden_sha256=hashlib.sha256(raw).hexdigest()[:16]))
     return recs
 
 
@@ -93,7 +96,8 @@ def _prefill(args):
     gpus = args.gpus or min(4, torch.cuda.device_count())
     job = BankJob(model=args.model, requests=args.requests, prompt_tokens=args.prompt_tokens,
                   chunk=args.chunk_size, transport="p2p" if args.transport == "segment-dma" else "nccl",
-                  profile=args.profile)
+                  profile=args.profile,
+                  resource_layout=options.get("additional_config", {}).get("qwen_infra_vpp_resource_layout", ""))
     with tempfile.TemporaryDirectory() as tmp:
         result = launch(job, gpus, Path(tmp) / "bank.pt")
     print(json.dumps(_records(result["outputs"], args.requests, result["tokens"]), indent=2))

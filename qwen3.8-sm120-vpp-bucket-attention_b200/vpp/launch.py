@@ -23,6 +23,7 @@ class BankJob:
     chunk: int = 2048
     transport: str = "p2p"  # or "nccl"
     profile: str = "vpp"  # or "cpp" (conventional pipeline, the comparison arm)
+    resource_layout: str = ""  # "rank" or "edge"; empty: the transport's default
     seed: int = 4321
     keep_all_outputs: bool = False
     banks: int = 1
@@ -64,7 +65,8 @@ def run_rank(job, rank, world, local_rank):
     transport = None
     if world > 1:
         transport = StageBoundaries(rank, world, dev, job.chunk, shape.hidden, backend=job.transport,
-                                    timeout=job.timeout_s, profile=job.profile)
+                                    timeout=job.timeout_s, profile=job.profile,
+                                    resource_layout=job.resource_layout or None)
     runner = FoldedRank(shape, rank, world, dev, job.tokens(), job.chunk, transport=transport,
                         keep_all_outputs=job.keep_all_outputs,
                         on_device_init=shape.hidden > 2048, profile=job.profile)

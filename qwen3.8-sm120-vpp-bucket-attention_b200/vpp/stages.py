@@ -1,11 +1,17 @@
 """Stage-boundary transport of one rank (the reference's ``StageBoundaries``,
 ``src/qwen_infra/vpp/native/stages.py:70-451``, rebuilt for NVLink).
 
-Rank-shared physical arenas: 2 source slots and 3 destination slots, each
-slot one message = 2 bf16 planes [capacity, H] (hidden at offset 0, residual
-at ``plane_bytes``).  Every directed wire edge also has a logical ring of 7
-ring slots with generation tickets (``native.SlotRing``) that validates the
-message lifecycle.
+A slot holds one message = 2 bf16 planes [capacity, H] (hidden at offset 0,
+residual at ``plane_bytes``).  Every directed wire edge has a logical ring of
+7 slots with generation tickets (``native.SlotRing``) that validates the
+message lifecycle.  Physical slots follow the resource layout
+(``vpp/native/stages.py:71-102``, ``docs/vpp-resources.md:70-93``):
+
+* ``"rank"`` (default for p2p): rank-shared arenas of 2 source and 3
+  destination slots that every edge of the rank leases one at a time;
+* ``"edge"`` (default, and the only layout, for nccl): every edge endpoint
+  owns its 7 slots, physical slot = ring slot (the reference's comparison
+  layout; 28 slots on a middle rank instead of 5).
 
 ``backend="p2p"`` (default): the destination arena is exported with CUDA IPC;
 the sender's copy stream copies both planes device-to-device straight into the
@@ -38,6 +44,72 @@ SOURCE_SLOTS = 2
 DEST_SLOTS = 3
 
 
+class _SharedSlots:
+    """Rank layout: ``count`` physical slots leased by every edge in turn."""
+
+    def __init__(self, count, stages):
+        self.count = count
+        self.leases = NV.PhysicalLeases(count)
+
+    def can_take(self, stage, seq):
+        return self.leases.available
+
+    def take(self, stage, ticket):
+        return self.leases.acquire(ticket)
+
+    def give_back(self, p, ticket):
+        self.leases.release(p, ticket)
+
+    def note_stall(self):
+        self.leases.note_stall()
+
+    @property
+    def peak(self):
+        return self.leases.peak_live
+
+    @property
+    def stalls(self):
+        return self.leases.stalls
+
+    def close(self):
+        self.leases.close()
+
+
+class _EdgeSlots:
+    """Edge layout: each edge endpoint owns RING_SLOTS physical slots; the
+    physical slot of a message is its ring slot."""
+
+    def __init__(self, count, stages):
+        self.base = {s: i * RING_SLOTS for i, s in enumerate(sorted(stages))}
+        self.count = RING_SLOTS * len(self.base)
+        self.owner = [None] * self.count
+        self.live = self.peak = self.stalls = 0
+
+    def can_take(self, stage, seq):
+        return self.owner[self.base[stage] + seq % RING_SLOTS] is None
+
+    def take(self, stage, ticket):
+        p = self.base[stage] + ticket.slot_id
+        if self.owner[p] is not None:
+            raise NV.BoundaryError("edge-owned slot still leased")
+        self.owner[p] = (ticket.ring_id, ticket.sequence, ticket.generation)
+        self.live += 1
+        self.peak = max(self.peak, self.live)
+        return p
+
+    def give_back(self, p, ticket):
+        if self.owner[p] != (ticket.ring_id, ticket.sequence, ticket.generation):
+            raise NV.BoundaryError("slot returned by a ticket that does not hold it")
+        self.owner[p] = None
+        self.live -= 1
+
+    def note_stall(self):
+        self.stalls += 1
+
+    def close(self):
+        pass
+
+
 class _Edge:
     def __init__(self, src_stage, ranks):
         self.src_stage = src_stage
@@ -66,11 +138,17 @@ def boundary_edges(rank, ranks, profile="vpp"):
 
 class StageBoundaries:
     def __init__(self, rank, ranks, device, capacity, hidden, *, backend="p2p", epoch=1, timeout=60.0,
-                 segment_bytes=16 << 20, control_group=None, session=None, profile="vpp"):
+                 segment_bytes=16 << 20, control_group=None, session=None, profile="vpp", resource_layout=None):
         if ranks < 2:
             raise ValueError("a boundary transport needs at least two ranks")
         if backend not in ("p2p", "nccl"):
             raise ValueError("backend is p2p or nccl")
+        resource_layout = resource_layout or ("rank" if backend == "p2p" else "edge")
+        if resource_layout not in ("rank", "edge"):
+            raise ValueError("resource layout is rank or edge")
+        if resource_layout == "rank" and backend != "p2p":
+            raise ValueError("rank-shared slots need the peer-to-peer transport")
+        self.resource_layout = resource_layout
         if profile not in L.PROFILES:
             raise ValueError("profile is vpp or cpp")
         self.rank, self.ranks, self.backend = rank, ranks, backend
@@ -89,22 +167,25 @@ class StageBoundaries:
         self.src_rings = {s: NV.SlotRing(NV.SOURCE, self.layout, epoch, e.src_stage) for s, e in self.out_edges.items()}
         self.dst_rings = {s: NV.SlotRing(NV.DESTINATION, self.layout, epoch, e.src_stage)
                           for s, e in self.in_edges.items()}
-        self.src_leases = NV.PhysicalLeases(SOURCE_SLOTS)
-        self.dst_leases = NV.PhysicalLeases(DEST_SLOTS)
+        slots = _SharedSlots if resource_layout == "rank" else _EdgeSlots
+        self.src_leases = slots(SOURCE_SLOTS, self.out_edges)
+        self.dst_leases = slots(DEST_SLOTS, self.in_edges)
+        n_src, n_dst = self.src_leases.count, max(1, self.dst_leases.count)
         self.out_seq = {s: 0 for s in self.out_edges}
         self.grant_seq = {s: 0 for s in self.in_edges}
         self.recv_seq = {s: 0 for s in self.in_edges}
         self.copy_stream = torch.cuda.Stream(device=self.device)
         # source slots: storage, ready events, copy-done events, owner
-        self.src_arena = torch.empty((SOURCE_SLOTS, 2, capacity, hidden), dtype=torch.bfloat16, device=self.device)
-        self.src_ready = [[torch.cuda.Event() for _ in range(2)] for _ in range(SOURCE_SLOTS)]
-        self.src_done = [torch.cuda.Event() for _ in range(SOURCE_SLOTS)]
-        self.src_busy = [None] * SOURCE_SLOTS  # (ticket, stage) until the copy out completes
-        self.res_marked = [False] * SOURCE_SLOTS
+        self.n_src, self.n_dst = n_src, n_dst
+        self.src_arena = torch.empty((n_src, 2, capacity, hidden), dtype=torch.bfloat16, device=self.device)
+        self.src_ready = [[torch.cuda.Event() for _ in range(2)] for _ in range(n_src)]
+        self.src_done = [torch.cuda.Event() for _ in range(n_src)]
+        self.src_busy = [None] * n_src  # (ticket, stage) until the copy out completes
+        self.res_marked = [False] * n_src
         self.src_current = {}  # (batch, stage) -> (physical, ticket)
         # destination slots
-        self.dst_done = [torch.cuda.Event() for _ in range(DEST_SLOTS)]
-        self.dst_busy = [None] * DEST_SLOTS  # ticket held until consumer done completes
+        self.dst_done = [torch.cuda.Event() for _ in range(n_dst)]
+        self.dst_busy = [None] * n_dst  # ticket held until consumer done completes
         self.dst_pending_free = set()
         self.grants = {}  # (stage, seq) -> (physical, ticket)
         self.schedule = []  # [(batch, stage)] receives in consumption order
@@ -124,10 +205,10 @@ class StageBoundaries:
             dist.broadcast_object_list(token, src=0, group=self.group)
             session = token[0]
         self.session = session
-        ptr, handle = NV.arena_alloc(self.dev_index, DEST_SLOTS * self.slot_bytes)
+        ptr, handle = NV.arena_alloc(self.dev_index, self.n_dst * self.slot_bytes)
         self.dst_ptr = ptr
-        self.dst_arena = torch.as_tensor(NV.DeviceBuffer(ptr, DEST_SLOTS * self.slot_bytes), device=self.device) \
-            .view(torch.bfloat16).view(DEST_SLOTS, 2, self.capacity, self.hidden)
+        self.dst_arena = torch.as_tensor(NV.DeviceBuffer(ptr, self.n_dst * self.slot_bytes), device=self.device) \
+            .view(torch.bfloat16).view(self.n_dst, 2, self.capacity, self.hidden)
         self.ctrl_in = {s: NV.ControlPage(self._ctrl_name(e), create=True) for s, e in self.in_edges.items()}
         self.ipc_out = {}
         out_handles = {}
@@ -155,7 +236,7 @@ class StageBoundaries:
     def _setup_nccl(self):
         self.session = None
         self.nccl_groups = (dist.new_group(backend="nccl"), dist.new_group(backend="nccl"))
-        self.dst_arena = torch.empty((DEST_SLOTS, 2, self.capacity, self.hidden), dtype=torch.bfloat16,
+        self.dst_arena = torch.empty((self.n_dst, 2, self.capacity, self.hidden), dtype=torch.bfloat16,
                                      device=self.device)
         self.nccl_sends = {}  # physical source slot -> works
 
@@ -176,8 +257,10 @@ class StageBoundaries:
         self._reap()
         if self.backend != "p2p":
             return
-        while self.sched_pos < len(self.schedule) and self.dst_leases.available:
+        while self.sched_pos < len(self.schedule):
             batch, stage = self.schedule[self.sched_pos]
+            if not self.dst_leases.can_take(stage, self.grant_seq[stage]):
+                break
             self._grant(batch, stage)
             self.sched_pos += 1
 
@@ -186,15 +269,15 @@ class StageBoundaries:
             if self.dst_done[p].query():
                 stage, ticket = self.dst_busy[p]
                 self.dst_rings[stage].transition(ticket, NV.OP_CONSUMER_COMPLETE)
-                self.dst_leases.release(p, ticket)
+                self.dst_leases.give_back(p, ticket)
                 self.dst_busy[p] = None
                 self.dst_pending_free.discard(p)
-        for p in range(SOURCE_SLOTS):
+        for p in range(self.n_src):
             busy = self.src_busy[p]
             if busy is not None and self._source_done(p):
                 stage, ticket = busy
                 self.src_rings[stage].transition(ticket, NV.OP_SOURCE_READ_COMPLETE)
-                self.src_leases.release(p, ticket)
+                self.src_leases.give_back(p, ticket)
                 self.src_busy[p] = None
 
     def _source_done(self, p):
@@ -209,7 +292,7 @@ class StageBoundaries:
         ticket = self.dst_rings[stage].try_acquire(d)
         if ticket is None:
             raise NV.BoundaryError("destination ring slot still busy")
-        p = self.dst_leases.acquire(ticket)
+        p = self.dst_leases.take(stage, ticket)
         self.dst_busy[p] = (stage, ticket)
         self.grants[(stage, seq)] = (p, ticket)
         self.ctrl_in[stage].grant(seq, p)
@@ -259,11 +342,11 @@ class StageBoundaries:
         ticket = ring.try_acquire(d)
         if ticket is None:
             raise NV.BoundaryError("source ring slot still busy")
-        if not self.src_leases.available:
+        if not self.src_leases.can_take(stage, seq):
             self.src_leases.note_stall()
             self.stats["slot_waits"] += 1
-            self._deadline_loop("a free source slot", lambda: self.src_leases.available)
-        p = self.src_leases.acquire(ticket)
+            self._deadline_loop("a free source slot", lambda: self.src_leases.can_take(stage, seq))
+        p = self.src_leases.take(stage, ticket)
         self.src_busy[p] = None
         self.src_current[(batch, stage)] = (p, ticket, d)
         return self.src_arena[p, 0, :rows], self.src_arena[p, 1, :rows]
@@ -343,11 +426,11 @@ class StageBoundaries:
             NV.cuda_check(NV.lib().qv_stream_wait_event(self.dev_index, compute.cuda_stream,
                                                         self.ipc_in[stage][seq % 8]), "wait for peer copy")
         else:
-            if not self.dst_leases.available:
-                self._deadline_loop("a free destination slot", lambda: self.dst_leases.available)
+            if not self.dst_leases.can_take(stage, seq):
+                self._deadline_loop("a free destination slot", lambda: self.dst_leases.can_take(stage, seq))
             d = self.layout.make(self.epoch, batch, seq, stage - 1, rows)
             ticket = self.dst_rings[stage].try_acquire(d)
-            p = self.dst_leases.acquire(ticket)
+            p = self.dst_leases.take(stage, ticket)
             self.dst_busy[p] = (stage, ticket)
             e = self.in_edges[stage]
             grp = self.nccl_groups[0 if e.forward else 1]
@@ -383,9 +466,10 @@ class StageBoundaries:
                 c.fail()
 
     def receipt(self):
-        return dict(self.stats, backend=self.backend, source_peak=self.src_leases.peak_live,
-                    dest_peak=self.dst_leases.peak_live, source_stalls=self.src_leases.stalls,
-                    arena_bytes=(SOURCE_SLOTS + DEST_SLOTS) * self.slot_bytes)
+        return dict(self.stats, backend=self.backend, resource_layout=self.resource_layout,
+                    source_peak=self.src_leases.peak, dest_peak=self.dst_leases.peak,
+                    source_stalls=self.src_leases.stalls,
+                    arena_bytes=(self.src_leases.count + self.dst_leases.count) * self.slot_bytes)
 
     def close(self):
         if self.closed:

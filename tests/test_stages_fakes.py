@@ -7,6 +7,7 @@ from types import SimpleNamespace
 import pytest
 
 from qwen_infra_b200.vpp import native as NV
+from qwen_infra_b200.vpp import stages as ST
 from qwen_infra_b200.vpp.stages import StageBoundaries
 
 
@@ -70,7 +71,7 @@ def test_grants_follow_consumption_order_and_slot_budget():
     t = _bare()
     # rank 1 of 3 receives stage 1 (edge 0 -> 1) and stage 4 (edge 3 -> 4)
     t.in_edges = {1: None, 4: None}
-    t.dst_leases = NV.PhysicalLeases(3)
+    t.dst_leases = ST._SharedSlots(3, t.in_edges)
     t.layout = NV.BoundaryLayout(64, 7, 3, 256)
     t.epoch, t.capacity = 1, 64
     t.dst_rings = {1: NV.SlotRing(NV.DESTINATION, t.layout, 1, 0), 4: NV.SlotRing(NV.DESTINATION, t.layout, 1, 3)}
@@ -82,3 +83,39 @@ def test_grants_follow_consumption_order_and_slot_budget():
     t.set_order([(0, 1), (1, 1), (0, 4), (2, 1), (1, 4), (3, 1)])
     assert granted == [(1, 0, 0), (1, 1, 1), (4, 0, 2)]
     assert t.schedule[t.sched_pos] == (2, 1)  # the next grant waits for a slot
+
+
+def test_edge_layout_grants_up_to_the_ring_on_each_edge():
+    """Edge-owned slots (the reference's comparison layout): each incoming
+    edge owns 7 physical slots, physical slot = edge base + ring slot, so
+    grants run ahead up to 7 per edge independently of the other edge."""
+    t = _bare()
+    t.in_edges = {1: None, 4: None}
+    t.dst_leases = ST._EdgeSlots(3, t.in_edges)
+    assert t.dst_leases.count == 14
+    t.layout = NV.BoundaryLayout(64, 7, 3, 256)
+    t.epoch, t.capacity = 1, 64
+    t.dst_rings = {1: NV.SlotRing(NV.DESTINATION, t.layout, 1, 0), 4: NV.SlotRing(NV.DESTINATION, t.layout, 1, 3)}
+    t.grant_seq = {1: 0, 4: 0}
+    t.grants, t.dst_busy = {}, [None] * 14
+    granted = []
+    t.ctrl_in = {s: SimpleNamespace(grant=lambda seq, p, s=s: granted.append((s, seq, p))) for s in (1, 4)}
+    t._reap = lambda: None
+    t.set_order([(b, 1) for b in range(9)] + [(b, 4) for b in range(2)])
+    assert granted == [(1, q, q) for q in range(7)]  # edge 1 stops at its 7 ring slots
+    # retire sequence 0 of edge 1: its slot (physical 0) comes back, the next grant proceeds
+    p, ticket = t.grants.pop((1, 0))
+    t.dst_rings[1].transition(ticket, NV.OP_TRANSFER_RECORDED)
+    t.dst_rings[1].transition(ticket, NV.OP_CONSUMER_RECORDED)
+    t.dst_rings[1].transition(ticket, NV.OP_CONSUMER_COMPLETE)
+    t.dst_leases.give_back(p, ticket)
+    t.progress()
+    assert granted[7] == (1, 7, 0)
+    assert t.dst_leases.peak == 7
+
+
+def test_resource_layout_rules():
+    with pytest.raises(ValueError):
+        StageBoundaries(0, 2, "cpu", 64, 256, backend="nccl", resource_layout="rank")
+    with pytest.raises(ValueError):
+        StageBoundaries(0, 2, "cpu", 64, 256, resource_layout="ring")
