@@ -126,6 +126,18 @@ class PagedKV:
         self.ks = torch.zeros(sshape, dtype=torch.uint8, device=device)
         self.vs = torch.zeros(sshape, dtype=torch.uint8, device=device)
 
+    @classmethod
+    def wrap(cls, k, v, ks, vs):
+        """A view over existing cache tensors (codes [pages, page, Hkv, D/2],
+        scales [pages, page, Hkv, D/16], uint8)."""
+        self = object.__new__(cls)
+        if k.dtype != torch.uint8 or k.ndim != 4 or v.shape != k.shape or ks.shape != vs.shape \
+                or ks.shape[:3] != k.shape[:3] or ks.shape[3] * 8 != k.shape[3]:
+            raise ValueError("expected NVFP4 caches [pages, page, Hkv, D/2] and scales [pages, page, Hkv, D/16]")
+        self.k, self.v, self.ks, self.vs = k, v, ks.view(torch.uint8), vs.view(torch.uint8)
+        self.page_size, self.kvheads, self.head_dim = k.shape[1], k.shape[2], k.shape[3] * 2
+        return self
+
     @property
     def pages(self):
         return self.k.shape[0]
@@ -206,6 +218,24 @@ def gate_fp8(out, gate, *, fp8=None, scale=None, head_dim=None, head_stride=None
                                                    _ptr(fp8), fp8.stride(0), _ptr(scale), rows, cols,
                                                    _stream(out.device))), "qi_gate_fp8_heads")
     return fp8, scale
+
+
+def gate_fp8_static(out, gate, scale, *, fp8=None, head_dim=None, head_stride=None):
+    """The reference's form of the FP8 epilogue: e4m3(bf16(out * bf16(sigmoid(gate))) / scale)
+    with one static fp32 device scalar ``scale``; gate addressing as :func:`gate_fp8`."""
+    _cuda(out, gate, scale)
+    rows, cols = out.shape
+    hd = cols if head_dim is None else head_dim
+    hs = 0 if head_stride is None else head_stride
+    if scale.dtype != torch.float32 or scale.numel() != 1:
+        raise ValueError("scale must be one fp32 device scalar")
+    if fp8 is None:
+        fp8 = torch.empty((rows, cols), dtype=torch.uint8, device=out.device)
+    N.check(_run("gate_fp8", rows * cols * 5, "B", out.device,
+                 lambda: N.lib().qi_gate_fp8_static(_ptr(out), _ptr(gate), out.stride(0), gate.stride(0), hs, hd,
+                                                    _ptr(fp8), fp8.stride(0), _ptr(scale), rows, cols,
+                                                    _stream(out.device))), "qi_gate_fp8_static")
+    return fp8
 
 
 def _gemm_struct(kind, epilogue, m, n, k, a, b, sfa=None, sfb=None, alpha=None, alpha_value=1.0):
