@@ -68,8 +68,11 @@ def parse():
     p.add_argument("--layers", type=int, default=None, help="override layer count (must split into 2N stages)")
     p.add_argument("--overlap", choices=("auto", "on", "off"), default="auto",
                    help="one GPU: run the two virtual stages on two CUDA streams (auto: on for N=1)")
+    p.add_argument("--attention", choices=("paged", "f16"), default="paged",
+                   help="paged: attention reads the NVFP4 cache directly (default); f16: the two-step comparison "
+                        "path (dequantise to f16 K/V^T, then attention)")
     p.add_argument("--kv-shadow", choices=("auto", "on", "off"), default="auto",
-                   help="keep each request's f16 K/V^T across its chunks (dequantise new tokens only)")
+                   help="--attention f16 only: keep each request's f16 K/V^T across its chunks")
     p.add_argument("--workload", choices=("prefill", "decode", "producers"), default="prefill",
                    help="prefill: the folded-VPP bank (default); decode: the bucket decode attention over the "
                         "paged NVFP4 cache (one query token per request, 1 GPU); producers: the fused-operator "
@@ -257,6 +260,7 @@ def run_ours(args):
     request_tokens = [args.prompt_tokens] * args.requests
     runner = FoldedRank(shape, rank, world, dev, request_tokens, args.chunk_size, transport=transport,
                         profile=args.profile, kv_shadow={"auto": None, "on": True, "off": False}[args.kv_shadow],
+                        attention=args.attention,
                         overlap={"auto": None, "on": True, "off": False}[args.overlap])
     gen = torch.Generator(device=dev).manual_seed(4321)
     embeds = [torch.randn(t, shape.hidden, generator=gen, device=dev).to(torch.bfloat16) for t in request_tokens] \

@@ -211,6 +211,30 @@ int qi_prefill_attention(const QiAttention* p, cudaStream_t stream);
  * SM count can ask for at this head_dim. */
 int qi_prefill_attention_workspace_bytes(int head_dim, int64_t* bytes);
 
+/* Causal GQA prefill attention straight over the paged NVFP4 cache: the
+ * kernel's producer warps load each 128-key tile's E2M1 codes and E4M3 scales
+ * through the block table and convert them to f16 in shared memory (no
+ * dequantised copy of the cache in HBM).  `rows` queries at positions
+ * history .. history+rows-1 attend keys 0 .. history+rows-1 of the request
+ * whose pages block_table lists (ceil((history+rows)/page_size) entries).
+ * page_size a power of two; head_dim 64 or 128; workspace as in QiAttention.
+ * Replaces the FlashInfer paged prefill selected at src/qwen_infra/config.py:80. */
+typedef struct QiPagedAttention {
+  const void* q; /* bf16 [rows, Hq*D] (row stride q_row elements) */
+  void* out;     /* bf16 [rows, Hq*D] (row stride out_row) */
+  QiKvView kv;
+  const int32_t* block_table;
+  const float *k_global, *v_global;
+  int* status;
+  int rows, history, qheads;
+  int64_t q_row, out_row;
+  float softmax_scale;
+  void* workspace;
+  int64_t workspace_bytes;
+} QiPagedAttention;
+
+int qi_paged_prefill_attention(const QiPagedAttention* p, cudaStream_t stream);
+
 /* qi_kv_dequant + qi_prefill_attention in one call that allocates nothing, for
  * callers that cannot allocate device memory (inside a graph capture or an
  * allocator callback, or a plugin host that only hands out input and output
@@ -278,10 +302,11 @@ int qi_nvfp4_quantize(const float* w, int64_t rows, int k, const float* global_s
 int qi_fp8_quantize_rows(const float* w, int rows, int k, void* q, float* scales, cudaStream_t stream);
 
 /* Conversion probe (tests): e2m1_pairs gets n/2 bytes packed pairwise and then
- * n/2 bytes packed eight at a time; e4m3[n]; ex[2n] = (fexp, sigmoid) pairs. */
+ * n/2 bytes packed eight at a time; e4m3[n]; ex[2n] = (expf, sigmoid) pairs. */
 int qi_convert_probe(const float* in, void* e2m1_pairs, void* e4m3, float* ex, int n, cudaStream_t stream);
 
-/* Host-only: sizeof(RefFront, QiFront, QiGemm, QiKvView, QiAttention, QiDecode) for ABI checks. */
+/* Host-only: sizeof(RefFront, QiFront, QiGemm, QiKvView, QiAttention, QiDecode, QiPagedAttention)
+ * for ABI checks (out[7]). */
 int qi_abi_struct_sizes(int* out);
 
 #ifdef __cplusplus

@@ -71,6 +71,16 @@ class QiAttention(ct.Structure):
     )
 
 
+class QiPagedAttention(ct.Structure):
+    _fields_ = (
+        [("q", _vp), ("out", _vp), ("kv", QiKvView), ("block_table", _vp), ("k_global", _vp), ("v_global", _vp),
+         ("status", _vp)]
+        + [(n, _i32) for n in ("rows", "history", "qheads")]
+        + [(n, _i64) for n in ("q_row", "out_row")]
+        + [("softmax_scale", _f32), ("workspace", _vp), ("workspace_bytes", _i64)]
+    )
+
+
 class QiDecode(ct.Structure):
     _fields_ = (
         [("q", _vp), ("kv", QiKvView)]
@@ -101,6 +111,7 @@ EXPORTS = {
     "qi_lm_head_argmax": ([_vp, _i64, _i32, _i32, _vp, _i32, _vp, _vp, _vp, _vp], _i32),
     "qi_lm_head_workspace_bytes": ([], _i32),
     "qi_prefill_attention": ([ct.POINTER(QiAttention), _vp], _i32),
+    "qi_paged_prefill_attention": ([ct.POINTER(QiPagedAttention), _vp], _i32),
     "qi_prefill_attention_workspace_bytes": ([_i32, ct.POINTER(_i64)], _i32),
     "qi_nvfp4_quantize": ([_vp, _i64, _i32, _vp, _vp, _vp, _vp], _i32),
     "qi_fp8_quantize_rows": ([_vp, _i32, _i32, _vp, _vp, _vp], _i32),
@@ -126,10 +137,11 @@ def lib():
             fn = getattr(handle, name)
             fn.argtypes = args
             fn.restype = res
-        sizes = (ct.c_int * 6)()
+        sizes = (ct.c_int * 7)()
         if handle.qi_abi_struct_sizes(sizes):
             raise RuntimeError("qi_abi_struct_sizes failed")
-        expected = [ct.sizeof(c) for c in (RefFront, QiFront, QiGemm, QiKvView, QiAttention, QiDecode)]
+        expected = [ct.sizeof(c) for c in (RefFront, QiFront, QiGemm, QiKvView, QiAttention, QiDecode,
+                                           QiPagedAttention)]
         if list(sizes) != expected:
             raise RuntimeError(f"C ABI struct sizes {list(sizes)} != ctypes {expected}")
         _lib = handle

@@ -59,6 +59,13 @@ struct AttnParams {
   unsigned* ws_count;  // [slots] arrival counters (parity = which piece is last)
   float* ws_ml;        // [slots][2][NQ*TQ][2] (m, l) per row and piece
   float* ws_o;         // [slots][2][NQ*TQ][HD] unnormalised O per row and piece
+  // Paged NVFP4 K/V (the paged kernel only): codes [page][entry][kv head][D/2]
+  // and E4M3 scales [..][D/16] through byte strides; keys past kv_tokens read
+  // as zeros.
+  const uint8_t *kc, *vc, *ksf, *vsf;
+  const int32_t* block_table;
+  int page_shift;
+  int64_t data_page, data_row, data_head, sf_page, sf_row, sf_head;
 };
 
 // Workspace of the key-range split for `slots` split units of head_dim hd.
@@ -189,11 +196,87 @@ QI_DEV void store_out_row(__nv_bfloat16* dst, const float* a, float norm, const 
   for (int i = 0; i < 4; ++i) o[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
 }
 
+// Roles.  f16 kernel (PAGED = false, 10 warps): warp 0 TMA producer, warp 1
+// TMEM allocator + MMA thread, warps 2..9 softmax.  Paged kernel (16 warps =
+// 4 warpgroups, one warp of each per SM sub-partition): warpgroup 0 the KV
+// producers (thread 0 also loads Q by TMA), warpgroups 1 and 2 the softmax of
+// the two query tiles, warp 12 the TMEM allocator + MMA thread (warps 13..15
+// idle).  The launch gives every thread 128 registers; setmaxnreg then moves
+// them to the softmax: producers 96, warpgroup 3 56, softmax 176 (per
+// sub-partition 96 + 2 x 176 + 56 = 504 <= 512; per CTA 128 x 96 + 128 x 56
+// + 256 x 176 = 64,512 <= 512 x 128 = 65,536).
+template <bool PAGED>
+struct Roles {
+  static constexpr int kThreads = PAGED ? 512 : 320;
+  static constexpr int kSoftFirst = PAGED ? 128 : 64;  // first softmax thread
+  static constexpr int kMmaWarp = PAGED ? 12 : 1;
+  static constexpr int kProducerWarps = PAGED ? 4 : 1;
+};
+
+// Paged producer: one thread handles QPK = HD/32 (key, 32-value quarter)
+// items of K and as many of V per key tile.  A tile's codes and scales are
+// loaded into registers one tile ahead; converting them writes f16 K and V
+// into the same shared-memory tiles the MMAs read: row kr of 128 bytes per
+// 64-value half of D, 16-byte chunks swizzled by kr & 7 (K-major K, MN-major V).
 template <int HD>
-__global__ void __launch_bounds__(320, 1)
+struct PagedTile {
+  static constexpr int QPK = HD / 32;
+  uint4 kc[QPK], vc[QPK];
+  uint32_t ks[QPK], vs[QPK];
+};
+
+template <int HD>
+QI_DEV void paged_fetch(const AttnParams& p, int kvh, int kbase, int t, PagedTile<HD>& b) {
+  constexpr int QPK = HD / 32;
+  const int qd = t % QPK;
+  const int page_mask = (1 << p.page_shift) - 1;
+#pragma unroll
+  for (int i = 0; i < QPK; ++i) {
+    const int token = kbase + i * (128 / QPK) + t / QPK;
+    if (token < p.kv_tokens) {
+      const int64_t page = __ldg(p.block_table + (token >> p.page_shift)), entry = token & page_mask;
+      const int64_t dofs = page * p.data_page + entry * p.data_row + (int64_t)kvh * p.data_head + qd * 16;
+      const int64_t sofs = page * p.sf_page + entry * p.sf_row + (int64_t)kvh * p.sf_head + qd * 2;
+      b.kc[i] = __ldg(reinterpret_cast<const uint4*>(p.kc + dofs));
+      b.vc[i] = __ldg(reinterpret_cast<const uint4*>(p.vc + dofs));
+      b.ks[i] = __ldg(reinterpret_cast<const unsigned short*>(p.ksf + sofs));
+      b.vs[i] = __ldg(reinterpret_cast<const unsigned short*>(p.vsf + sofs));
+    } else {
+      b.kc[i] = b.vc[i] = make_uint4(0, 0, 0, 0);
+      b.ks[i] = b.vs[i] = 0;
+    }
+  }
+}
+
+// e2m1 x e4m3 -> f16 (exact) into a [D/64][128 keys][128 B] swizzled tile.
+template <int HD>
+QI_DEV void paged_put(const uint4* codes, const uint32_t* scales, uint8_t* tile, int t) {
+  constexpr int QPK = HD / 32;
+  const int qd = t % QPK;
+#pragma unroll
+  for (int i = 0; i < QPK; ++i) {
+    const int kr = i * (128 / QPK) + t / QPK;
+    const uint32_t s2 = e4m3x2_to_f16x2(scales[i] & 0xFFFFu);
+    const uint32_t words[4] = {codes[i].x, codes[i].y, codes[i].z, codes[i].w};
+    uint8_t* row = tile + (qd >> 1) * (128 * 128) + kr * 128;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {  // 16-byte output chunk c: elements 8c .. 8c+7 of the quarter
+      uint32_t f[4];
+      e2m1x8_to_f16x8(words[c], f);
+      const uint32_t sc = splat_half(s2, c >> 1);
+      const int chunk = ((qd & 1) * 4 + c) ^ (kr & 7);
+      *reinterpret_cast<uint4*>(row + chunk * 16) =
+          make_uint4(hmul2u(f[0], sc), hmul2u(f[1], sc), hmul2u(f[2], sc), hmul2u(f[3], sc));
+    }
+  }
+}
+
+template <int HD, bool PAGED>
+__global__ void __launch_bounds__(Roles<PAGED>::kThreads, 1)
     attn_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                 const __grid_constant__ CUtensorMap tv, AttnParams p) {
   using G = Geometry<HD>;
+  using R = Roles<PAGED>;
   constexpr int Q_TILE = G::Q_TILE, K_BYTES = G::K_BYTES, V_BYTES = G::V_BYTES, V_ATOM = G::V_ATOM;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -232,14 +315,17 @@ __global__ void __launch_bounds__(320, 1)
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&tq);
-    prefetch_tensormap(&tk);
-    prefetch_tensormap(&tv);
+    if constexpr (!PAGED) {
+      prefetch_tensormap(&tk);
+      prefetch_tensormap(&tv);
+    }
     mbar_init(q_full, 1);
     mbar_init(q_ready, NQ * 4);  // one arrival per softmax warp
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&k_full[i], 1);
+      // TMA: one expect_tx arrival; paged: one arrival per producer warp
+      mbar_init(&k_full[i], R::kProducerWarps);
       mbar_init(&k_empty[i], 1);
-      mbar_init(&v_full[i], 1);
+      mbar_init(&v_full[i], R::kProducerWarps);
       mbar_init(&v_empty[i], 1);
     }
     for (int i = 0; i < NQ; ++i) {
@@ -251,34 +337,14 @@ __global__ void __launch_bounds__(320, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  if (warp == R::kMmaWarp) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    if (lane == 0) {
-      mbar_expect_tx(q_full, NQ * Q_TILE);
-#pragma unroll
-      for (int t = 0; t < NQ; ++t)
-#pragma unroll
-        for (int a = 0; a < HD / 64; ++a)
-          tma_load_2d(sQ + t * Q_TILE + a * ATOM, &tq, q_full, head * HD + 64 * a, q0 + t * TQ);
-      for (int j = 0; j < ntiles; ++j) {
-        const int s = j & 1;
-        if (j >= 2 && !mbar_wait(&k_empty[s], ((j >> 1) - 1) & 1, abort_flag, p.status)) break;
-        mbar_expect_tx(&k_full[s], K_BYTES);
-#pragma unroll
-        for (int a = 0; a < HD / 64; ++a)
-          tma_load_3d(sK + s * K_BYTES + a * ATOM, &tk, &k_full[s], 64 * a, (j_first + j) * TK, kvh);
-        if (j >= 2 && !mbar_wait(&v_empty[s], ((j >> 1) - 1) & 1, abort_flag, p.status)) break;
-        mbar_expect_tx(&v_full[s], V_BYTES);
-        tma_load_3d(sV + s * V_BYTES, &tv, &v_full[s], (j_first + j) * TK, 0, kvh);
-        tma_load_3d(sV + s * V_BYTES + V_ATOM, &tv, &v_full[s], (j_first + j) * TK + 64, 0, kvh);
-      }
-    }
-  } else if (warp == 1) {
+  // Role bodies (one per kind of warp), dispatched below by warpgroup.
+  auto mma_role = [&]() {
     if (lane == 0) {
       // Issue order: S0_0 S1_0 | PV0_0 S0_1 PV1_0 S1_1 | PV0_1 S0_2 ... (each PV
       // in two halves of 64 keys, the first as soon as its P is stored) so that
@@ -288,7 +354,9 @@ __global__ void __launch_bounds__(320, 1)
       // execute in order, so the read precedes the overwrite.  The commit that
       // signals S_t(j+1) covers PV_t(j) as well, so the softmax may rescale O
       // once it sees S_t(j+1).
-      constexpr uint32_t idesc_s = idesc_f16(128), idesc_o = idesc_f16(HD);
+      // PV reads V^T K-major (f16 kernel) or V in its natural [key][D] order
+      // as an MN-major B operand (paged kernel: instruction-descriptor bit 16).
+      constexpr uint32_t idesc_s = idesc_f16(128), idesc_o = idesc_f16(HD) | (PAGED ? (1u << 16) : 0u);
       const uint32_t q_base = smem_u32(sQ);
       bool ok = mbar_wait(q_ready, 0, abort_flag, p.status);
       tc_fence_after();
@@ -308,8 +376,14 @@ __global__ void __launch_bounds__(320, 1)
         const uint32_t a_p = tmem + (t ? G::S_COL1 : G::S_COL0), d_o = tmem + (t ? G::O_COL1 : G::O_COL0);
 #pragma unroll
         for (int kk = 4 * h; kk < 4 * h + 4; ++kk) {
-          const uint32_t voff = (kk >> 2) * V_ATOM + (kk & 3) * 32;
-          mma_f16_ts(d_o, a_p + kk * 8, sdesc_kmajor_sw128(v_base + voff), idesc_o, (j | kk) ? 1u : 0u);
+          uint64_t vdesc;
+          if constexpr (PAGED) {
+            // 16 keys = 16 rows of 128 B; the D halves 16 KB apart; 8-row groups 1 KB apart
+            vdesc = sdesc_mnmajor_sw128(v_base + kk * 2048, 128 * 128, 1024);
+          } else {
+            vdesc = sdesc_kmajor_sw128(v_base + (kk >> 2) * V_ATOM + (kk & 3) * 32);
+          }
+          mma_f16_ts(d_o, a_p + kk * 8, vdesc, idesc_o, (j | kk) ? 1u : 0u);
         }
       };
       if (ok && (ok = mbar_wait(&k_full[0], 0, abort_flag, p.status))) {
@@ -347,8 +421,9 @@ __global__ void __launch_bounds__(320, 1)
         tc_commit(&pv_done[1]);
       }
     }
-  } else {
-    const int t = (warp - 2) >> 2;      // query tile of this warpgroup
+  };
+  auto softmax_role = [&]() {
+    const int t = (warp - R::kSoftFirst / 32) >> 2;  // query tile of this warpgroup
     const int quarter = warp & 3;       // TMEM lane quarter
     const int r = quarter * 32 + lane;  // row within the tile == TMEM lane
     const int qrow = q0 + t * TQ + r;
@@ -360,7 +435,7 @@ __global__ void __launch_bounds__(320, 1)
     bool ok = mbar_wait(q_full, 0, abort_flag, p.status);
     if (ok) {
       uint4* q4 = reinterpret_cast<uint4*>(sQ + t * Q_TILE);
-      for (int i = (int)threadIdx.x - 64 - t * 128; i < Q_TILE / 16; i += 128) {
+      for (int i = (int)threadIdx.x - R::kSoftFirst - t * 128; i < Q_TILE / 16; i += 128) {
         uint4 v = q4[i];
         uint32_t* w = reinterpret_cast<uint32_t*>(&v);
 #pragma unroll
@@ -502,7 +577,7 @@ __global__ void __launch_bounds__(320, 1)
       __threadfence();
       named_bar_sync(1, NQ * TQ);
       volatile int* last_flag = abort_flag + 1;
-      if (threadIdx.x == 64) {
+      if (threadIdx.x == R::kSoftFirst) {
         const unsigned old = atomicAdd(p.ws_count + slot, 1u);
         __threadfence();
         *last_flag = (int)(old & 1u);
@@ -540,10 +615,81 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
     }
+  };
+  if constexpr (PAGED) {
+    if (warp < 4) {
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 104;");
+      const int t = threadIdx.x;  // 0 .. 127
+      if (t == 0) {
+        mbar_expect_tx(q_full, NQ * Q_TILE);
+  #pragma unroll
+        for (int qt = 0; qt < NQ; ++qt)
+  #pragma unroll
+          for (int a = 0; a < HD / 64; ++a)
+            tma_load_2d(sQ + qt * Q_TILE + a * ATOM, &tq, q_full, head * HD + 64 * a, q0 + qt * TQ);
+      }
+      // Tile j: wait until the MMAs that read stage j & 1 two tiles ago are
+      // done, convert, make the generic-proxy writes visible to the tensor
+      // cores, then one arrival per warp.  Tile j + 1 is loaded first.
+      auto step = [&](PagedTile<HD>& cur, PagedTile<HD>& nxt, int j) -> bool {
+        if (j + 1 < ntiles) paged_fetch<HD>(p, kvh, (j_first + j + 1) * TK, t, nxt);
+        const int s = j & 1;
+        if (j >= 2 && !mbar_wait(&k_empty[s], ((j >> 1) - 1) & 1, abort_flag, p.status)) return false;
+        paged_put<HD>(cur.kc, cur.ks, sK + s * K_BYTES, t);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&k_full[s]);
+        if (j >= 2 && !mbar_wait(&v_empty[s], ((j >> 1) - 1) & 1, abort_flag, p.status)) return false;
+        paged_put<HD>(cur.vc, cur.vs, sV + s * V_BYTES, t);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&v_full[s]);
+        return true;
+      };
+      PagedTile<HD> ta, tb;
+      if (ntiles > 0) paged_fetch<HD>(p, kvh, j_first * TK, t, ta);
+      for (int j = 0; j < ntiles; j += 2) {
+        if (!step(ta, tb, j)) break;
+        if (j + 1 < ntiles && !step(tb, ta, j + 1)) break;
+      }
+    } else if (warp >= 12) {
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 72;");
+      if (warp == 12) mma_role();  // warps 13..15 only take part in the CTA barriers
+    } else {
+      asm volatile("setmaxnreg.inc.sync.aligned.u32 168;");
+      softmax_role();
+    }
+  } else {
+    if (warp == 0) {
+      if (lane == 0) {
+        mbar_expect_tx(q_full, NQ * Q_TILE);
+  #pragma unroll
+        for (int t = 0; t < NQ; ++t)
+  #pragma unroll
+          for (int a = 0; a < HD / 64; ++a)
+            tma_load_2d(sQ + t * Q_TILE + a * ATOM, &tq, q_full, head * HD + 64 * a, q0 + t * TQ);
+        for (int j = 0; j < ntiles; ++j) {
+          const int s = j & 1;
+          if (j >= 2 && !mbar_wait(&k_empty[s], ((j >> 1) - 1) & 1, abort_flag, p.status)) break;
+          mbar_expect_tx(&k_full[s], K_BYTES);
+  #pragma unroll
+          for (int a = 0; a < HD / 64; ++a)
+            tma_load_3d(sK + s * K_BYTES + a * ATOM, &tk, &k_full[s], 64 * a, (j_first + j) * TK, kvh);
+          if (j >= 2 && !mbar_wait(&v_empty[s], ((j >> 1) - 1) & 1, abort_flag, p.status)) break;
+          mbar_expect_tx(&v_full[s], V_BYTES);
+          tma_load_3d(sV + s * V_BYTES, &tv, &v_full[s], (j_first + j) * TK, 0, kvh);
+          tma_load_3d(sV + s * V_BYTES + V_ATOM, &tv, &v_full[s], (j_first + j) * TK + 64, 0, kvh);
+        }
+      }
+    } else if (warp == 1) {
+      mma_role();
+    } else {
+      softmax_role();
+    }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == R::kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -616,30 +762,63 @@ int split_plan(int units, int sms, int lightest_tiles, int slots_available) {
   return k < slots_available ? k : slots_available;
 }
 
-template <int HD>
-int launch_attention(const QiAttention* a, cudaStream_t stream) {
-  CUtensorMap mq, mk, mv;
-  const uint64_t qd[2] = {(uint64_t)a->q_row, (uint64_t)a->rows};
-  const uint64_t qs[1] = {(uint64_t)a->q_row * 2};
-  const uint64_t kd[3] = {(uint64_t)HD, (uint64_t)a->kv_tokens, (uint64_t)a->kvheads};
-  const uint64_t ks[2] = {(uint64_t)HD * 2, (uint64_t)a->kv_tokens * HD * 2};
-  const uint64_t vd[3] = {(uint64_t)a->kv_tokens, (uint64_t)HD, (uint64_t)a->kvheads};
-  const uint64_t vs[2] = {(uint64_t)a->vt_row * 2, (uint64_t)a->vt_row * HD * 2};
-  if (!make_map16(&mq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a->q, 2, qd, qs, 128) ||
-      !make_map16(&mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->k, 3, kd, ks, 128) ||
-      !make_map16(&mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->vt, 3, vd, vs, HD))
-    return (int)cudaErrorInvalidValue;
+// Key-range split plan, workspace carve-up and launch, shared by both kernels.
+template <int HD, bool PAGED>
+int run_attention(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, AttnParams p,
+                  void* workspace, int64_t workspace_bytes, cudaStream_t stream) {
   static bool configured[64] = {};
   int cur_dev = 0;
   cudaGetDevice(&cur_dev);
   if (cur_dev < 0 || cur_dev >= 64) return (int)cudaErrorInvalidDevice;
   const int sms = sm_count(cur_dev);
   if (!configured[cur_dev]) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(attn_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, Geometry<HD>::SMEM);
+    const cudaError_t e = cudaFuncSetAttribute(attn_kernel<HD, PAGED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               Geometry<HD>::SMEM);
     if (e != cudaSuccess) return (int)e;
     configured[cur_dev] = true;
   }
+  p.q_blocks = (p.rows + NQ * TQ - 1) / (NQ * TQ);
+  const int units = p.q_blocks * p.qheads;
+  int slots_available = 0;
+  if (workspace && workspace_bytes > 0) {
+    int lo = 0, hi = units < kMaxSlots ? units : kMaxSlots;  // largest slot count whose workspace fits
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) / 2;
+      if (ws_bytes(mid, HD) <= workspace_bytes) lo = mid; else hi = mid - 1;
+    }
+    slots_available = lo;
+  }
+  const int lightest_tiles = (p.history + (p.rows < NQ * TQ ? p.rows : NQ * TQ) + TK - 1) / TK;
+  const int split = split_plan(units, sms, lightest_tiles, slots_available);
+  p.split_first = units - split;
+  if (split) {
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    p.ws_count = reinterpret_cast<unsigned*>(ws);
+    p.ws_ml = reinterpret_cast<float*>(ws + ws_count_bytes(split));
+    p.ws_o = reinterpret_cast<float*>(ws + ws_count_bytes(split) + ws_ml_bytes(split));
+  }
+  attn_kernel<HD, PAGED><<<units + split, Roles<PAGED>::kThreads, Geometry<HD>::SMEM, stream>>>(mq, mk, mv, p);
+  return (int)cudaPeekAtLastError();
+}
+
+template <int HD>
+bool make_q_map(CUtensorMap* mq, const void* q, int64_t q_row, int rows) {
+  const uint64_t qd[2] = {(uint64_t)q_row, (uint64_t)rows};
+  const uint64_t qs[1] = {(uint64_t)q_row * 2};
+  return make_map16(mq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, q, 2, qd, qs, 128);
+}
+
+template <int HD>
+int launch_attention(const QiAttention* a, cudaStream_t stream) {
+  CUtensorMap mq, mk, mv;
+  const uint64_t kd[3] = {(uint64_t)HD, (uint64_t)a->kv_tokens, (uint64_t)a->kvheads};
+  const uint64_t ks[2] = {(uint64_t)HD * 2, (uint64_t)a->kv_tokens * HD * 2};
+  const uint64_t vd[3] = {(uint64_t)a->kv_tokens, (uint64_t)HD, (uint64_t)a->kvheads};
+  const uint64_t vs[2] = {(uint64_t)a->vt_row * 2, (uint64_t)a->vt_row * HD * 2};
+  if (!make_q_map<HD>(&mq, a->q, a->q_row, a->rows) ||
+      !make_map16(&mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->k, 3, kd, ks, 128) ||
+      !make_map16(&mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a->vt, 3, vd, vs, HD))
+    return (int)cudaErrorInvalidValue;
   AttnParams p{};
   p.rows = a->rows;
   p.history = a->history;
@@ -652,28 +831,40 @@ int launch_attention(const QiAttention* a, cudaStream_t stream) {
   p.v_global = a->v_global;
   p.softmax_scale = a->softmax_scale;
   p.status = a->status;
-  p.q_blocks = (a->rows + NQ * TQ - 1) / (NQ * TQ);
-  const int units = p.q_blocks * a->qheads;
-  int slots_available = 0;
-  if (a->workspace && a->workspace_bytes > 0) {
-    int lo = 0, hi = units < kMaxSlots ? units : kMaxSlots;  // largest slot count whose workspace fits
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) / 2;
-      if (ws_bytes(mid, HD) <= a->workspace_bytes) lo = mid; else hi = mid - 1;
-    }
-    slots_available = lo;
-  }
-  const int lightest_tiles = (a->history + (a->rows < NQ * TQ ? a->rows : NQ * TQ) + TK - 1) / TK;
-  const int split = split_plan(units, sms, lightest_tiles, slots_available);
-  p.split_first = units - split;
-  if (split) {
-    uint8_t* ws = static_cast<uint8_t*>(a->workspace);
-    p.ws_count = reinterpret_cast<unsigned*>(ws);
-    p.ws_ml = reinterpret_cast<float*>(ws + ws_count_bytes(split));
-    p.ws_o = reinterpret_cast<float*>(ws + ws_count_bytes(split) + ws_ml_bytes(split));
-  }
-  attn_kernel<HD><<<units + split, 320, Geometry<HD>::SMEM, stream>>>(mq, mk, mv, p);
-  return (int)cudaPeekAtLastError();
+  return run_attention<HD, false>(mq, mk, mv, p, a->workspace, a->workspace_bytes, stream);
+}
+
+template <int HD>
+int launch_paged_attention(const QiPagedAttention* a, cudaStream_t stream) {
+  CUtensorMap mq;
+  CUtensorMap unused{};
+  if (!make_q_map<HD>(&mq, a->q, a->q_row, a->rows)) return (int)cudaErrorInvalidValue;
+  const QiKvView& kv = a->kv;
+  AttnParams p{};
+  p.rows = a->rows;
+  p.history = a->history;
+  p.kv_tokens = a->history + a->rows;
+  p.qheads = a->qheads;
+  p.group = a->qheads / kv.kvheads;
+  p.out_row = a->out_row;
+  p.out = static_cast<__nv_bfloat16*>(a->out);
+  p.k_global = a->k_global;
+  p.v_global = a->v_global;
+  p.softmax_scale = a->softmax_scale;
+  p.status = a->status;
+  p.kc = static_cast<const uint8_t*>(kv.k_cache);
+  p.vc = static_cast<const uint8_t*>(kv.v_cache);
+  p.ksf = static_cast<const uint8_t*>(kv.k_scales);
+  p.vsf = static_cast<const uint8_t*>(kv.v_scales);
+  p.block_table = a->block_table;
+  p.page_shift = __builtin_ctz((unsigned)kv.page_size);
+  p.data_page = kv.data_page;
+  p.data_row = kv.data_row;
+  p.data_head = kv.data_head;
+  p.sf_page = kv.sf_page;
+  p.sf_row = kv.sf_row;
+  p.sf_head = kv.sf_head;
+  return run_attention<HD, true>(mq, unused, unused, p, a->workspace, a->workspace_bytes, stream);
 }
 
 }  // namespace
@@ -691,12 +882,37 @@ bool attention_request_valid(const QiAttention* a) {
   return aligned16(a->q) && aligned16(a->k) && aligned16(a->vt) && aligned16(a->out) &&
          !(a->workspace && (reinterpret_cast<uintptr_t>(a->workspace) & 255));
 }
+bool paged_attention_request_valid(const QiPagedAttention* a) {
+  if (!a || a->rows < 1 || a->history < 0 || a->qheads < 1 || !a->q || !a->out || !a->block_table ||
+      !a->k_global || !a->v_global)
+    return false;
+  const QiKvView& kv = a->kv;
+  if ((kv.head_dim != 64 && kv.head_dim != 128) || kv.kvheads < 1 || a->qheads % kv.kvheads || kv.page_size < 1 ||
+      (kv.page_size & (kv.page_size - 1)) || !kv.k_cache || !kv.v_cache || !kv.k_scales || !kv.v_scales)
+    return false;
+  const int64_t hd = kv.head_dim;
+  if ((int64_t)a->history + a->rows > (int64_t)1 << 30 || a->q_row % 8 || a->out_row % 8 ||
+      a->q_row < a->qheads * hd || a->out_row < a->qheads * hd)
+    return false;
+  // 16-byte code loads and 2-byte scale loads per 32 values of a key
+  return aligned16(a->q) && aligned16(a->out) && aligned16(kv.k_cache) && aligned16(kv.v_cache) &&
+         !(kv.data_page % 16) && !(kv.data_row % 16) && !(kv.data_head % 16) &&
+         !(reinterpret_cast<uintptr_t>(kv.k_scales) & 1) && !(reinterpret_cast<uintptr_t>(kv.v_scales) & 1) &&
+         !(kv.sf_page % 2) && !(kv.sf_row % 2) && !(kv.sf_head % 2) &&
+         !(a->workspace && (reinterpret_cast<uintptr_t>(a->workspace) & 255));
+}
 }  // namespace qi
 
 extern "C" int qi_prefill_attention(const QiAttention* a, cudaStream_t stream) {
   QI_BIND(stream, a ? a->q : nullptr);
   if (!attention_request_valid(a)) return (int)cudaErrorInvalidValue;
   return a->head_dim == 64 ? launch_attention<64>(a, stream) : launch_attention<128>(a, stream);
+}
+
+extern "C" int qi_paged_prefill_attention(const QiPagedAttention* a, cudaStream_t stream) {
+  QI_BIND(stream, a ? a->q : nullptr);
+  if (!paged_attention_request_valid(a)) return (int)cudaErrorInvalidValue;
+  return a->kv.head_dim == 64 ? launch_paged_attention<64>(a, stream) : launch_paged_attention<128>(a, stream);
 }
 
 extern "C" int qi_prefill_attention_workspace_bytes(int head_dim, int64_t* bytes) {

@@ -256,6 +256,14 @@ QI_DEV uint64_t sdesc_kmajor_sw128(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
+// MN-major operand with 128-byte swizzle: 64-element MN chunks of 128 B,
+// 8 K-rows per 1 KB atom; LBO = stride between MN chunks, SBO = stride
+// between 8-row K groups.
+__device__ __forceinline__ uint64_t sdesc_mnmajor_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
 QI_DEV void tc_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
@@ -345,10 +353,44 @@ QI_DEV bool elect_one() {
   return pred != 0;
 }
 
+// NVFP4 / E4M3 -> f16 conversions of the cached K/V values (exact in f16).
+// Two e2m1 codes (one byte, low nibble = even element) -> f16x2 (even in the
+// low half); four bytes of a word at once.
+__device__ __forceinline__ void e2m1x8_to_f16x8(uint32_t w, uint32_t* out) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(out[0]), "=r"(out[1]), "=r"(out[2]), "=r"(out[3])
+      : "r"(w));
+}
+// Two e4m3 scale bytes (low byte first) -> f16x2.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two) {
+  uint32_t out;
+  asm("{\n\t.reg .b16 h;\n\t"
+      "cvt.u16.u32 h, %1;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, h;\n\t}"
+      : "=r"(out)
+      : "r"(two));
+  return out;
+}
+__device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+// f16x2 with the low (sel = 0) or high (sel = 1) half of `pair` in both halves.
+__device__ __forceinline__ uint32_t splat_half(uint32_t pair, int sel) {
+  return sel ? __byte_perm(pair, 0, 0x3232) : __byte_perm(pair, 0, 0x1010);
+}
+
 // Host-side request checks shared by entry points that combine several
 // launches (the allocation-free attention): every argument is checked before
 // the first launch, so a rejected call launches nothing.
 bool attention_request_valid(const QiAttention* a);
+bool paged_attention_request_valid(const QiPagedAttention* a);
 bool kv_dequant_request_valid(const QiKvView* kv, const int32_t* block_table, int first, int tokens,
                               const void* k_out, int64_t k_capacity, const void* vt_out, int64_t vt_row);
 

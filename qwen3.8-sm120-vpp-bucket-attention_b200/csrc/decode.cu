@@ -167,38 +167,6 @@ __global__ void __launch_bounds__(128) assign_kernel(const int32_t* __restrict__
 // Compute helpers
 // ---------------------------------------------------------------------------
 
-// Two e2m1 codes (one byte, low nibble = even element) -> f16x2 (even in the
-// low half); four bytes of a word at once.
-__device__ __forceinline__ void e2m1x8_to_f16x8(uint32_t w, uint32_t* out) {
-  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
-      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
-      : "=r"(out[0]), "=r"(out[1]), "=r"(out[2]), "=r"(out[3])
-      : "r"(w));
-}
-// Two e4m3 scale bytes (low byte first) -> f16x2.
-__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two) {
-  uint32_t out;
-  asm("{\n\t.reg .b16 h;\n\t"
-      "cvt.u16.u32 h, %1;\n\t"
-      "cvt.rn.f16x2.e4m3x2 %0, h;\n\t}"
-      : "=r"(out)
-      : "r"(two));
-  return out;
-}
-__device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-// f16x2 with the low (sel = 0) or high (sel = 1) half of `pair` in both halves.
-__device__ __forceinline__ uint32_t splat_half(uint32_t pair, int sel) {
-  return sel ? __byte_perm(pair, 0, 0x3232) : __byte_perm(pair, 0, 0x1010);
-}
-
 // 32 lanes x 8 columns (register i -> column taddr + i).
 __device__ __forceinline__ void tmem_st8w(uint32_t taddr, const uint32_t* v) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
@@ -261,14 +229,6 @@ __device__ __forceinline__ void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint3
 constexpr uint32_t kIdescS = idesc_nvfp4(kQTerms * kMaxGroup);
 constexpr uint32_t kIdescO =
     (1u << 4) | (1u << 15) | ((uint32_t)(kMaxGroup >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-
-// MN-major operand with 128-byte swizzle: 64-element MN chunks of 128 B,
-// 8 K-rows per 1 KB atom; LBO = stride between MN chunks, SBO = stride
-// between 8-row K groups.
-__device__ __forceinline__ uint64_t sdesc_mnmajor_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
-         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
 
 // Byte offset of element (row, k) in a K-major SW128 operand of 16 rows whose
 // K extent is split into 64-element blocks of 2 KB (16 rows x 128 B).

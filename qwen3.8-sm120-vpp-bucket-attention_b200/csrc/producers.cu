@@ -841,6 +841,7 @@ int qi_abi_struct_sizes(int* out) {
   out[3] = (int)sizeof(QiKvView);
   out[4] = (int)sizeof(QiAttention);
   out[5] = (int)sizeof(QiDecode);
+  out[6] = (int)sizeof(QiPagedAttention);
   return 0;
 }
 

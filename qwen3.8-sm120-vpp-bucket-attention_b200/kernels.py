@@ -419,6 +419,35 @@ def prefill_attention(q, k, vt, *, history, qheads, kvheads, head_dim, k_global,
     return out
 
 
+def paged_prefill_attention(q, kv, block_table, *, history, qheads, k_global, v_global, out=None,
+                            softmax_scale=None, status=None, workspace=None):
+    """Causal GQA attention of ``rows`` queries at positions history.. over the
+    request's keys 0 .. history+rows-1, read straight from the paged NVFP4
+    cache ``kv`` (a :class:`PagedKV`) through ``block_table``.  ``workspace``:
+    the key-range split workspace (default: the device's cached one)."""
+    _cuda(q, block_table, k_global, v_global)
+    d = kv.head_dim
+    if workspace is None:
+        workspace = attention_workspace(q.device, d)
+    rows = q.shape[0]
+    if block_table.dtype != torch.int32 or block_table.numel() * kv.page_size < history + rows:
+        raise ValueError("block_table: int32 with a page for every key")
+    if out is None:
+        out = torch.empty((rows, qheads * d), dtype=torch.bfloat16, device=q.device)
+    p = N.QiPagedAttention()
+    p.q, p.out, p.kv, p.block_table = q.data_ptr(), out.data_ptr(), kv.view(), block_table.data_ptr()
+    p.k_global, p.v_global = k_global.data_ptr(), v_global.data_ptr()
+    p.status = status.data_ptr() if status is not None else None
+    p.rows, p.history, p.qheads = rows, history, qheads
+    p.q_row, p.out_row = q.stride(0), out.stride(0)
+    p.softmax_scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(d)
+    p.workspace, p.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    N.check(_run("attention", 4 * qheads * d * (rows * history + rows * (rows + 1) // 2), "FLOP", q.device,
+                 lambda: N.lib().qi_paged_prefill_attention(ct.byref(p), _stream(q.device))),
+            "qi_paged_prefill_attention")
+    return out
+
+
 def nvfp4_quantize(w, global_scale, *, q=None, scales=None):
     """fp32 [rows, K] -> NVFP4 codes [rows, K/2] + swizzled scales."""
     _cuda(w, global_scale)

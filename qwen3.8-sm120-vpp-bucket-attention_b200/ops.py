@@ -177,10 +177,8 @@ def paged_prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
                             v_scales: torch.Tensor, block_table: torch.Tensor, k_global: torch.Tensor,
                             v_global: torch.Tensor, history: int, qheads: int) -> torch.Tensor:
     kv = K.PagedKV.wrap(k_cache, v_cache, k_scales, v_scales)
-    rows = q.shape[0]
-    k, vt = K.kv_dequant(kv, block_table, history + rows)
-    return K.prefill_attention(q, k, vt, history=history, qheads=qheads, kvheads=kv.kvheads,
-                               head_dim=kv.head_dim, k_global=k_global, v_global=v_global)
+    return K.paged_prefill_attention(q, kv, block_table, history=history, qheads=qheads, k_global=k_global,
+                                     v_global=v_global)
 
 
 @paged_prefill_attention.register_fake

@@ -187,7 +187,10 @@ class StageModel:
     for every request of a bank, and the stage forward."""
 
     def __init__(self, shape, layers, device, *, max_rows, request_tokens, base_seed=1234, on_device_init=None,
-                 final_norm=False, kv_shadow=None, streams=1):
+                 final_norm=False, kv_shadow=None, streams=1, attention="paged"):
+        if attention not in ("paged", "f16"):
+            raise ValueError("attention is paged or f16")
+        self.attention = attention
         self.shape = shape
         self.device = torch.device(device)
         self.layers = list(layers)
@@ -205,7 +208,8 @@ class StageModel:
         self.rope = rope_table(self.max_tokens, s.head_dim, s.rope_theta, self.device)
         # One workspace per concurrently running stage (streams=2: the two
         # virtual stages of a rank overlap on two CUDA streams).
-        self.ws_sets = [Workspace(s, max_rows, self.max_tokens, self.device) for _ in range(streams)]
+        self.ws_sets = [Workspace(s, max_rows, self.max_tokens if attention == "f16" else 0, self.device)
+                        for _ in range(streams)]
         self.ws = self.ws_sets[0]
         f = lambda v: torch.tensor([v], dtype=torch.float32, device=self.device)
         self.g_norm, self.g_down = f(ACT_GLOBAL_NORM), f(ACT_GLOBAL_DOWN)
@@ -217,12 +221,17 @@ class StageModel:
             self.lm_head = _seeded_normal((s.vocab, s.hidden), base_seed + LM_HEAD_SEED_OFFSET, 0.02, self.device,
                                           on_device_init).to(torch.bfloat16)
         self.softmax_scale = 1.0 / math.sqrt(s.head_dim)
-        # f16 K / V^T of each (request, layer) kept across the request's chunks,
-        # so every chunk dequantises only its own new tokens (instead of the
-        # whole history again); on when all of them fit in a third of the free
-        # memory.  Zero-filled: keys past the current length read as 0.
+        # attention="f16" only (the two-step comparison path): f16 K / V^T of
+        # each (request, layer) kept across the request's chunks, so every
+        # chunk dequantises only its own new tokens (instead of the whole
+        # history again); on when all of them fit in a third of the free
+        # memory.  Zero-filled: keys past the current length read as 0.  The
+        # default paged attention reads the NVFP4 cache itself and keeps no
+        # copy.
         self.request_tokens = list(request_tokens)
-        if kv_shadow is None:
+        if attention == "paged":
+            kv_shadow = False
+        elif kv_shadow is None:
             need = sum(2 * s.kvheads * ((t + 63) // 64 * 64) * s.head_dim * 2 for t in request_tokens) * len(self.layers)
             kv_shadow = self.device.type == "cuda" and need < torch.cuda.mem_get_info(self.device)[0] // 3
         self.kv_shadow = bool(kv_shadow)
@@ -261,18 +270,23 @@ class StageModel:
                                    self.vg, qheads=s.qheads, kvheads=s.kvheads, head_dim=d, eps=s.eps,
                                    q=ws.q[:rows], want_gate=False, status=ws.status)
         tokens = ctx.history + rows
-        if self.kv_shadow:
-            kd, vt = self._shadow(ctx, layer)
-            K.kv_dequant(kv, ctx.block_table, tokens, first=ctx.history // 64 * 64, k_out=kd, vt_out=vt)
+        attn_ws = ws.attn_ws if split else ws.attn_ws[:0]
+        if self.attention == "paged":
+            att = K.paged_prefill_attention(q, kv, ctx.block_table, history=ctx.history, qheads=s.qheads,
+                                            k_global=self.kg, v_global=self.vg, out=ws.att[:rows],
+                                            softmax_scale=self.softmax_scale, status=ws.status, workspace=attn_ws)
         else:
-            kd, vt = ws.kv_views(s, tokens)
-            K.kv_dequant(kv, ctx.block_table, tokens, k_out=kd, vt_out=vt)
-        att = K.prefill_attention(q, kd, vt, history=ctx.history, qheads=s.qheads, kvheads=s.kvheads, head_dim=d,
-                                  k_global=self.kg, v_global=self.vg, out=ws.att[:rows],
-                                  softmax_scale=self.softmax_scale, status=ws.status,
-                                  workspace=ws.attn_ws if split else ws.attn_ws[:0])
-        if self.kv_shadow and tokens >= self.request_tokens[ctx.request]:
-            del self.shadow[(ctx.request, layer)]  # last chunk: stream order keeps the buffers until read
+            if self.kv_shadow:
+                kd, vt = self._shadow(ctx, layer)
+                K.kv_dequant(kv, ctx.block_table, tokens, first=ctx.history // 64 * 64, k_out=kd, vt_out=vt)
+            else:
+                kd, vt = ws.kv_views(s, tokens)
+                K.kv_dequant(kv, ctx.block_table, tokens, k_out=kd, vt_out=vt)
+            att = K.prefill_attention(q, kd, vt, history=ctx.history, qheads=s.qheads, kvheads=s.kvheads,
+                                      head_dim=d, k_global=self.kg, v_global=self.vg, out=ws.att[:rows],
+                                      softmax_scale=self.softmax_scale, status=ws.status, workspace=attn_ws)
+            if self.kv_shadow and tokens >= self.request_tokens[ctx.request]:
+                del self.shadow[(ctx.request, layer)]  # last chunk: stream order keeps the buffers until read
         a8, s8 = K.gate_fp8(att, qkv[:, d:], fp8=ws.a8[:rows], scale=ws.s8[:rows], head_dim=d, head_stride=2 * d)
         o = K.gemm_e4m3(a8, w.o_q, m=rows, n=h, k=s.qheads * d, row_scale=s8, col_scale=w.o_scale,
                         out=ws.o[:rows])

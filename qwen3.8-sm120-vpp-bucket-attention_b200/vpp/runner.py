@@ -47,7 +47,8 @@ class FoldedRank:
     stage rank of G, output on rank G-1."""
 
     def __init__(self, shape, rank, ranks, device, request_tokens, chunk, *, transport=None, base_seed=1234,
-                 on_device_init=None, keep_all_outputs=False, profile="vpp", kv_shadow=None, overlap=None):
+                 on_device_init=None, keep_all_outputs=False, profile="vpp", kv_shadow=None, overlap=None,
+                 attention="paged"):
         if profile not in L.PROFILES:
             raise ValueError("profile is vpp or cpp")
         self.shape, self.rank, self.ranks, self.profile = shape, rank, ranks, profile
@@ -78,7 +79,7 @@ class FoldedRank:
         self.overlap = can if overlap is None else (bool(overlap) and can)
         self.model = StageModel(shape, layers, self.device, max_rows=chunk, request_tokens=self.request_tokens,
                                 base_seed=base_seed, on_device_init=on_device_init,
-                                final_norm=(rank == self.output_rank), kv_shadow=kv_shadow,
+                                final_norm=(rank == self.output_rank), kv_shadow=kv_shadow, attention=attention,
                                 streams=2 if self.overlap else 1)
         self.transport = transport
         self.keep_all_outputs = keep_all_outputs
