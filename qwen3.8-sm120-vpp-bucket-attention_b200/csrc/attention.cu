@@ -202,9 +202,9 @@ QI_DEV void store_out_row(__nv_bfloat16* dst, const float* a, float norm, const 
 // producers (thread 0 also loads Q by TMA), warpgroups 1 and 2 the softmax of
 // the two query tiles, warp 12 the TMEM allocator + MMA thread (warps 13..15
 // idle).  The launch gives every thread 128 registers; setmaxnreg then moves
-// them to the softmax: producers 96, warpgroup 3 56, softmax 176 (per
-// sub-partition 96 + 2 x 176 + 56 = 504 <= 512; per CTA 128 x 96 + 128 x 56
-// + 256 x 176 = 64,512 <= 512 x 128 = 65,536).
+// them to the softmax: producers 120, warpgroup 3 72, softmax 160 (per
+// sub-partition 120 + 2 x 160 + 72 = 512; per CTA 128 x 120 + 256 x 160 +
+// 128 x 72 = 65,536 = 512 x 128).  This split compiles without spills.
 template <bool PAGED>
 struct Roles {
   static constexpr int kThreads = PAGED ? 512 : 320;
@@ -214,7 +214,7 @@ struct Roles {
 };
 
 // Paged producer: one thread handles QPK = HD/32 (key, 32-value quarter)
-// items of K and as many of V per key tile.  A tile's codes and scales are
+// items of K and as many of V per key tile (mapping: paged_key / paged_quarter).  A tile's codes and scales are
 // loaded into registers one tile ahead; converting them writes f16 K and V
 // into the same shared-memory tiles the MMAs read: row kr of 128 bytes per
 // 64-value half of D, 16-byte chunks swizzled by kr & 7 (K-major K, MN-major V).
@@ -225,14 +225,30 @@ struct PagedTile {
   uint32_t ks[QPK], vs[QPK];
 };
 
+// Item i of producer thread t: key i * (128/QPK) + (t / 32) * KPW + t % KPW,
+// quarter (t % 32) / KPW, KPW = 32/QPK keys per warp and pass.  Consecutive
+// lanes take consecutive keys, so each quarter-warp's eight 16-byte shared
+// stores land on eight different swizzle positions (no bank conflict), and a
+// warp's loads still cover whole 64-byte key rows.
+template <int HD>
+QI_DEV int paged_key(int i, int t) {
+  constexpr int QPK = HD / 32, KPW = 32 / QPK;
+  return i * (128 / QPK) + (t >> 5) * KPW + (t & 31) % KPW;
+}
+template <int HD>
+QI_DEV int paged_quarter(int t) {
+  constexpr int KPW = 32 / (HD / 32);
+  return (t & 31) / KPW;
+}
+
 template <int HD>
 QI_DEV void paged_fetch(const AttnParams& p, int kvh, int kbase, int t, PagedTile<HD>& b) {
   constexpr int QPK = HD / 32;
-  const int qd = t % QPK;
+  const int qd = paged_quarter<HD>(t);
   const int page_mask = (1 << p.page_shift) - 1;
 #pragma unroll
   for (int i = 0; i < QPK; ++i) {
-    const int token = kbase + i * (128 / QPK) + t / QPK;
+    const int token = kbase + paged_key<HD>(i, t);
     if (token < p.kv_tokens) {
       const int64_t page = __ldg(p.block_table + (token >> p.page_shift)), entry = token & page_mask;
       const int64_t dofs = page * p.data_page + entry * p.data_row + (int64_t)kvh * p.data_head + qd * 16;
@@ -252,10 +268,10 @@ QI_DEV void paged_fetch(const AttnParams& p, int kvh, int kbase, int t, PagedTil
 template <int HD>
 QI_DEV void paged_put(const uint4* codes, const uint32_t* scales, uint8_t* tile, int t) {
   constexpr int QPK = HD / 32;
-  const int qd = t % QPK;
+  const int qd = paged_quarter<HD>(t);
 #pragma unroll
   for (int i = 0; i < QPK; ++i) {
-    const int kr = i * (128 / QPK) + t / QPK;
+    const int kr = paged_key<HD>(i, t);
     const uint32_t s2 = e4m3x2_to_f16x2(scales[i] & 0xFFFFu);
     const uint32_t words[4] = {codes[i].x, codes[i].y, codes[i].z, codes[i].w};
     uint8_t* row = tile + (qd >> 1) * (128 * 128) + kr * 128;
@@ -618,7 +634,7 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads, 1)
   };
   if constexpr (PAGED) {
     if (warp < 4) {
-      asm volatile("setmaxnreg.dec.sync.aligned.u32 104;");
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 120;");
       const int t = threadIdx.x;  // 0 .. 127
       if (t == 0) {
         mbar_expect_tx(q_full, NQ * Q_TILE);
@@ -656,7 +672,7 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads, 1)
       asm volatile("setmaxnreg.dec.sync.aligned.u32 72;");
       if (warp == 12) mma_role();  // warps 13..15 only take part in the CTA barriers
     } else {
-      asm volatile("setmaxnreg.inc.sync.aligned.u32 168;");
+      asm volatile("setmaxnreg.inc.sync.aligned.u32 160;");
       softmax_role();
     }
   } else {
