@@ -54,7 +54,8 @@ def parse():
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--model", choices=("qwen27b", "tiny"), default="qwen27b")
     p.add_argument("--requests", type=int, default=4)
-    p.add_argument("--prompt-tokens", type=int, default=32768)
+    p.add_argument("--prompt-tokens", default="32768",
+                   help="tokens per request, or a comma-separated list (one request each)")
     p.add_argument("--chunk-size", type=int, default=2048)
     p.add_argument("--transport", choices=("p2p", "nccl"), default="p2p")
     p.add_argument("--resource-layout", choices=("rank", "edge"), default=None,
@@ -151,48 +152,92 @@ class ClockSampler:
 # CPU legs: the oracle (CPU restatement of the reference semantics)
 # ---------------------------------------------------------------------------
 
-def cpu_sample(args, threads):
-    """Time the oracle's layer forward for one chunk at history 0 and at the
-    longest history of the bank; extrapolate to a bank by the cost model
-    t(h) = a + b * attention_pairs(h) summed over every chunk and layer."""
+def request_tokens(args):
+    """Prompt lengths of the bank: ``--prompt-tokens N`` for ``--requests``
+    requests of N tokens, or a comma-separated list (one request each, e.g.
+    the mixed 8192,32768,65536,131072 bank)."""
+    vals = [int(v) for v in str(args.prompt_tokens).split(",") if v]
+    if not vals or min(vals) < 1:
+        raise SystemExit("--prompt-tokens: positive token counts")
+    return vals if len(vals) > 1 else vals * args.requests
+
+
+def _pairs(h, rows):
+    return rows * h + rows * (rows + 1) // 2
+
+
+def cpu_bank_exact(args, threads):
+    """Time the oracle's forward of the whole bank on the host: every layer of
+    every chunk of every request (the final norm and LM head excluded).  Used
+    for the tiny model (config 1), where it takes seconds."""
     import numpy as np
     import torch
+    from oracle import formats as F
     from oracle import model as OM
 
     torch.set_num_threads(threads)
     shape = OM.QWEN27B if args.model == "qwen27b" else OM.TINY
+    layers = list(range(args.layers or shape.layers))
+    rng = np.random.default_rng(3)
+    c = args.chunk_size
+    total = 0.0
+    for t in request_tokens(args):
+        m = OM.OracleModel(shape, layers, t)  # weights and KV built outside the timed region
+        x = F.bf16_round(rng.standard_normal((t, shape.hidden)).astype(np.float32))
+        t0 = time.perf_counter()
+        for start in range(0, t, c):
+            h, r = x[start:start + c], None
+            for l in layers:
+                h, r = m.layer(l, h, r, start)
+        total += time.perf_counter() - t0
+    tokens = sum(request_tokens(args))
+    return dict(value=tokens / total, unit="tok/s", cores=threads, kind="port", extrapolated=False,
+                sample=f"oracle forward of the whole bank: {len(request_tokens(args))} request(s), "
+                       f"{tokens} tokens, chunk {c}, {len(layers)} layers ({total:.1f} s, timed end to end)",
+                bank_seconds=total)
+
+
+def cpu_sample(args, threads):
+    """The CPU baseline of the bank.  Tiny model: the whole bank, timed
+    (cpu_bank_exact).  27B shape: the oracle's layer forward for one chunk at
+    history 0 and at the longest history of the bank, extrapolated to the bank
+    with the cost model t(h) = a + b * attention_pairs(h) over every chunk and
+    layer (a bank would take days on the host); the line says so."""
+    if args.model == "tiny":
+        return cpu_bank_exact(args, threads)
+    import numpy as np
+    import torch
+    from oracle import formats as F
+    from oracle import model as OM
+
+    torch.set_num_threads(threads)
+    shape = OM.QWEN27B
     layers = args.layers or shape.layers
     c = args.chunk_size
-    hist_long = max(0, (args.prompt_tokens - 1) // c * c)
-    max_tokens = hist_long + c
-    m = OM.OracleModel(shape, [0], max_tokens)
+    reqs = request_tokens(args)
+    hist_long = max(0, (max(reqs) - 1) // c * c)
+    m = OM.OracleModel(shape, [0], hist_long + c)
     rng = np.random.default_rng(3)
-    x = rng.standard_normal((c, shape.hidden)).astype(np.float32)
-    from oracle import formats as F
-
-    x = F.bf16_round(x)
+    x = F.bf16_round(rng.standard_normal((c, shape.hidden)).astype(np.float32))
     times = {}
     for hist in (0, hist_long):
         t0 = time.perf_counter()
         m.layer(0, x, x, hist)
         times[hist] = time.perf_counter() - t0
-
-    def pairs(h, rows):
-        return rows * h + rows * (rows + 1) // 2
-
-    p0, p1 = pairs(0, c), pairs(hist_long, c)
+    p0, p1 = _pairs(0, c), _pairs(hist_long, c)
     b = (times[hist_long] - times[0]) / (p1 - p0) if p1 > p0 else 0.0
     a = times[0] - b * p0
     total = 0.0
-    for r in range(args.requests):
-        for start in range(0, args.prompt_tokens, c):
-            rows = min(c, args.prompt_tokens - start)
-            total += (a * rows / c + b * pairs(start, rows)) * layers
-    tokens = args.requests * args.prompt_tokens
+    for t in reqs:
+        for start in range(0, t, c):
+            rows = min(c, t - start)
+            total += (a * rows / c + b * _pairs(start, rows)) * layers
+    tokens = sum(reqs)
     sample = (f"oracle layer forward, 1 layer x {c} rows at history 0 and {hist_long} "
-              f"({times[0]:.1f} s + {times[hist_long]:.1f} s), extrapolated to {args.requests}x{args.prompt_tokens} "
-              f"tokens x {layers} layers (extrapolated)")
-    return dict(value=tokens / total, unit="tok/s", cores=threads, kind="port", sample=sample,
+              f"({times[0]:.1f} s + {times[hist_long]:.1f} s), extrapolated to {len(reqs)} requests / {tokens} "
+              f"tokens x {layers} layers by t = a + b * attention pairs")
+    return dict(value=tokens / total, unit="tok/s", cores=threads, kind="port", extrapolated=True,
+                sample=sample, sample_seconds=[times[0], times[hist_long]], fit=dict(a_s=a, b_s_per_pair=b),
                 bank_seconds=total)
 
 
@@ -207,20 +252,27 @@ def run_reference(args):
         base = cpu_sample(args, threads)
         steps.append(base["bank_seconds"])
     bank_s = statistics.median(steps)
-    tokens = args.requests * args.prompt_tokens
+    reqs = request_tokens(args)
+    tokens = sum(reqs)
     value = tokens / bank_s
+    cpu = {k: v for k, v in base.items() if k != "bank_seconds"}
+    cpu["value"] = value
     line = dict(
         metric=METRIC, value=value, unit="tok/s", n_gpus=args.gpus, steps=args.steps, warmup=args.warmup,
         ms_per_step=bank_s * 1e3, higher_is_better=True, scaling="strong", vs_baseline=None, dtype="f32",
-        data="synthetic", impl="reference",
-        config=dict(workload=f"{args.model} {args.requests}x{args.prompt_tokens} chunk {args.chunk_size}",
-                    model=args.model, requests=args.requests, prompt_tokens=args.prompt_tokens,
+        data="synthetic", impl="reference", extrapolated=base["extrapolated"],
+        config=dict(workload=_workload(args, reqs), model=args.model, requests=len(reqs), prompt_tokens=reqs,
                     chunk=args.chunk_size),
-        cpu_baseline=dict(value=value, unit="tok/s", cores=threads, kind="port", sample=base["sample"]),
+        cpu_baseline=cpu,
         e2e=dict(value=value, unit="tok/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0),
     )
     print(json.dumps(line), flush=True)
     return 0
+
+
+def _workload(args, reqs):
+    lens = f"{len(reqs)}x{reqs[0]}" if len(set(reqs)) == 1 else "+".join(str(t) for t in reqs)
+    return f"{args.model} {lens} tokens, chunk {args.chunk_size}"
 
 
 # ---------------------------------------------------------------------------
@@ -257,13 +309,13 @@ def run_ours(args):
 
         transport = StageBoundaries(rank, world, dev, args.chunk_size, shape.hidden, backend=args.transport,
                                     profile=args.profile, resource_layout=args.resource_layout)
-    request_tokens = [args.prompt_tokens] * args.requests
-    runner = FoldedRank(shape, rank, world, dev, request_tokens, args.chunk_size, transport=transport,
+    reqs = request_tokens(args)
+    runner = FoldedRank(shape, rank, world, dev, reqs, args.chunk_size, transport=transport,
                         profile=args.profile, kv_shadow={"auto": None, "on": True, "off": False}[args.kv_shadow],
                         attention=args.attention,
                         overlap={"auto": None, "on": True, "off": False}[args.overlap])
     gen = torch.Generator(device=dev).manual_seed(4321)
-    embeds = [torch.randn(t, shape.hidden, generator=gen, device=dev).to(torch.bfloat16) for t in request_tokens] \
+    embeds = [torch.randn(t, shape.hidden, generator=gen, device=dev).to(torch.bfloat16) for t in reqs] \
         if rank == 0 else None
     torch.cuda.synchronize()
 
@@ -330,7 +382,7 @@ def run_ours(args):
     e2e = None
     if not args.no_e2e:
         host = [e.cpu().pin_memory() for e in embeds] if rank == 0 else None
-        out_host = torch.empty(args.requests, dtype=torch.int32).pin_memory()  # the output token ids
+        out_host = torch.empty(len(reqs), dtype=torch.int32).pin_memory()  # the output token ids
         runner.run_bank(None, host_embeds=host)
         torch.cuda.synchronize()
         barrier()
@@ -345,9 +397,9 @@ def run_ours(args):
         torch.cuda.synchronize()
         barrier()
         e2e_ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
-        tokens = args.requests * args.prompt_tokens
+        tokens = sum(reqs)
         e2e = dict(value=tokens / (e2e_ms / 1e3), unit="tok/s", ms_per_step=e2e_ms,
-                   h2d_bytes_per_step=tokens * shape.hidden * 2, d2h_bytes_per_step=args.requests * 4)
+                   h2d_bytes_per_step=tokens * shape.hidden * 2, d2h_bytes_per_step=len(reqs) * 4)
 
     if rank != 0:
         if transport is not None:
@@ -355,12 +407,12 @@ def run_ours(args):
         dist.destroy_process_group()
         return 0
 
-    tokens = args.requests * args.prompt_tokens
+    tokens = sum(reqs)
     peaks, peak_kind = load_peaks()
     total_flops = tokens * shape.linear_flops_per_token() * shape.layers
-    for r in range(args.requests):
-        for start in range(0, args.prompt_tokens, args.chunk_size):
-            rows = min(args.chunk_size, args.prompt_tokens - start)
+    for t in reqs:
+        for start in range(0, t, args.chunk_size):
+            rows = min(args.chunk_size, t - start)
             total_flops += shape.attention_flops(start, rows) * shape.layers
     kernels = {}
     for name, d in kernel_summary.items():
@@ -391,8 +443,7 @@ def run_ours(args):
             bound = "tensor"
         traffic = traffic_source = None
         if dom_name == "attention" and args.model == "qwen27b" and args.chunk_size == ATTN_TRAFFIC_ROWS:
-            keys = [start + min(args.chunk_size, args.prompt_tokens - start)
-                    for _ in range(args.requests) for start in range(0, args.prompt_tokens, args.chunk_size)]
+            keys = [start + min(args.chunk_size, t - start) for t in reqs for start in range(0, t, args.chunk_size)]
             traffic = ATTN_TRAFFIC_BYTES * (sum(keys) / len(keys)) / ATTN_TRAFFIC_KEYS
             traffic_source = ("ncu capture (profiles/attention_27b_chunk2048_history30720.md), scaled by the keys "
                               "of each launch; bytes per launch, averaged over the bank")
@@ -407,15 +458,15 @@ def run_ours(args):
         warmup=args.warmup, ms_per_step=ms, bank_latency_ms=ms, higher_is_better=True, scaling="strong",
         vs_baseline=None, dtype="nvfp4 (e2m1 x e4m3/16, fp32 accum), fp8 O-proj, bf16 attention",
         data="synthetic (seeded embeddings, random-init weights of the architecture)",
-        config=dict(workload=f"{args.model} {args.requests}x{args.prompt_tokens} tokens, chunk {args.chunk_size}, "
+        config=dict(workload=_workload(args, reqs) + ", "
                              + (f"{2 * world} virtual stages on {world} GPU(s)" if args.profile == "vpp"
                                 else f"conventional {world}-stage pipeline"),
                     profile=args.profile,
-                    model=args.model, layers=shape.layers, requests=args.requests,
-                    prompt_tokens=args.prompt_tokens, chunk=args.chunk_size,
+                    model=args.model, layers=shape.layers, requests=len(reqs),
+                    prompt_tokens=reqs, chunk=args.chunk_size,
                     virtual_stages=2 * world if args.profile == "vpp" else world,
                     parallelism=f"folded-vpp pp{world}" if args.profile == "vpp" else f"pp{world}", transport=(args.transport if world > 1 else "local fold"),
-                    stage_streams=2 if runner.overlap else 1,
+                    stage_streams=2 if runner.overlap else 1, attention=args.attention,
                     l2="inputs larger than L2 (weights ~16 GB, KV pages)"),
         bubble_fraction=bubble, busiest_rank_compute_ms=busiest, instrumented_bank_ms=makespan,
         model_tflops=total_flops / (ms / 1e3) / 1e12,
