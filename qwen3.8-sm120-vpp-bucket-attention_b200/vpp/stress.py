@@ -1,0 +1,171 @@
+"""Stage-boundary transport exerciser (the reference's transport stress
+benchmark, ``benchmarks/vpp_resources.py:84-204``, on this build's
+``StageBoundaries``).
+
+Every rank walks its folded rank-local order (``layout.rank_local_stage_orders``)
+for ``messages`` batches with no model: a stage's "output" is its input planes
+refilled with a payload identity -- hidden = the batch id, residual = the
+source stage -- and every receive checks on the GPU that the planes carry
+exactly that, so a message that lands in the wrong slot, arrives stale or is
+torn shows up as mismatching elements.  Valid rows cycle through
+{0, 1, 17, C/2, C} (a 0-row boundary included), which exercises ragged
+copies, slot wrap-around (7-slot rings, 2 source / 3 destination physical
+slots) and the final drain.
+
+``timed=True`` instead sends full-capacity messages and measures, with CUDA
+events on the sending rank's copy stream, the bytes copied per second over
+NVLink (both planes: 2 x C x H x 2 bytes per message).
+
+    python -m qwen_infra_b200.vpp.stress --gpus 2 [--backend p2p|nccl] [--timed]
+
+One process per GPU (spawned here), NCCL process group, gloo control plane.
+"""
+
+import argparse
+import json
+import os
+import socket
+import tempfile
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from . import layout as L
+
+ROWS_CYCLE = ("0", "1", "17", "C/2", "C")
+
+
+def rows_for(batch, capacity, timed):
+    if timed:
+        return capacity
+    pick = ROWS_CYCLE[batch % len(ROWS_CYCLE)]
+    return {"0": 0, "1": 1, "17": 17, "C/2": capacity // 2, "C": capacity}[pick]
+
+
+def run_rank(rank, world, device, *, capacity, hidden, messages, backend="p2p", resource_layout=None,
+             timed=False, timeout=60.0):
+    """One rank's walk; returns its receipt with ``mismatches`` (elements that
+    differed from the payload identity), ``received`` and, when timed, the
+    copy rate of its outgoing messages."""
+    from .stages import StageBoundaries
+
+    if timed and backend != "p2p":
+        raise ValueError("timed copies are measured on the peer-to-peer transport's copy stream")
+    G = world
+    last = 2 * G - 1
+    transport = StageBoundaries(rank, world, device, capacity, hidden, backend=backend, timeout=timeout,
+                                resource_layout=resource_layout)
+    order = L.rank_local_stage_orders(list(range(messages)), G)[rank]
+    transport.set_order(order)
+    bad = torch.zeros((), dtype=torch.int64, device=device)
+    fold = torch.empty((2, capacity, hidden), dtype=torch.bfloat16, device=device)
+    received = 0
+    sent_bytes = 0
+    ev = None
+    for batch, stage in order:
+        rows = rows_for(batch, capacity, timed)
+        if stage == 0:
+            pass  # the first stage has no input boundary
+        elif stage == G:  # local fold on rank G-1
+            h, r = fold[0, :rows], fold[1, :rows]
+            bad += (h != batch).sum() + (r != G - 1).sum()
+        else:
+            h, r = transport.receive(batch, stage, rows)
+            if not timed:
+                bad += (h != batch).sum() + (r != stage - 1).sum()
+            transport.retire(batch, stage)
+            received += 1
+        if stage == last:
+            continue
+        if stage == G - 1:
+            fold[0, :rows].fill_(batch)
+            fold[1, :rows].fill_(stage)
+            continue
+        hp, rp = transport.prepare_send(batch, stage, rows)
+        rp.fill_(stage)
+        transport.mark_residual_ready(batch, stage)
+        hp.fill_(batch)
+        if timed and ev is None and batch >= 2:  # after two warm-up messages per edge
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(transport.copy_stream)
+            sent_bytes = 0
+        transport.send(batch, stage, rows)
+        if ev is not None:
+            sent_bytes += 2 * rows * hidden * 2
+    end = None
+    if timed and ev is not None:
+        end = torch.cuda.Event(enable_timing=True)
+        end.record(transport.copy_stream)
+    torch.cuda.synchronize(device)
+    receipt = transport.close()
+    receipt.update(rank=rank, mismatches=int(bad.item()), received=received, messages=messages,
+                   capacity=capacity, hidden=hidden)
+    if end is not None:
+        ms = ev.elapsed_time(end)
+        receipt.update(copy_ms=ms, copy_bytes=sent_bytes, copy_gbs=sent_bytes / (ms / 1e3) / 1e9 if ms > 0 else None)
+    return receipt
+
+
+def _worker(rank, world, port, kwargs, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=timedelta(seconds=kwargs.get("timeout", 60.0) + 30))
+    try:
+        receipt = run_rank(rank, world, dev, **kwargs)
+        Path(out_dir, f"rank{rank}.json").write_text(json.dumps(receipt))
+    finally:
+        dist.destroy_process_group()
+
+
+def launch(world, **kwargs):
+    """Spawn ``world`` ranks (GPU i for rank i); returns their receipts."""
+    if world < 2 or world > torch.cuda.device_count():
+        raise ValueError(f"needs 2 .. {torch.cuda.device_count()} GPUs, asked {world}")
+    import __graft_entry__
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    with tempfile.TemporaryDirectory() as out_dir:
+        ctx = mp.get_context("spawn")
+        procs = [ctx.Process(target=__graft_entry__.spawn_call, args=("qwen_infra_b200.vpp.stress", "_worker",
+                                                                      r, world, port, kwargs, out_dir))
+                 for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=kwargs.get("timeout", 60.0) * 4 + 120)
+        codes = [p.exitcode for p in procs]
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+        if any(c != 0 for c in codes):
+            raise RuntimeError(f"stress ranks exited with {codes}")
+        return [json.loads(Path(out_dir, f"rank{r}.json").read_text()) for r in range(world)]
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(prog="qwen_infra_b200.vpp.stress")
+    ap.add_argument("--gpus", type=int, default=2)
+    ap.add_argument("--capacity", type=int, default=2048)
+    ap.add_argument("--hidden", type=int, default=5120)
+    ap.add_argument("--messages", type=int, default=20)
+    ap.add_argument("--backend", choices=("p2p", "nccl"), default="p2p")
+    ap.add_argument("--resource-layout", choices=("rank", "edge"), default=None)
+    ap.add_argument("--timed", action="store_true")
+    a = ap.parse_args(argv)
+    receipts = launch(a.gpus, capacity=a.capacity, hidden=a.hidden, messages=a.messages, backend=a.backend,
+                      resource_layout=a.resource_layout, timed=a.timed)
+    for r in receipts:
+        print(json.dumps(r))
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -28,7 +28,8 @@ def test_two_rank_fold_matches_single_gpu_bit_exact(tmp_path, transport):
     for b in one:
         assert torch.equal(one[b], two["outputs"][b]), b
     receipt = two["receipt"]
-    assert receipt["source_peak"] <= 2 and receipt["dest_peak"] <= 3
+    budget = (2, 3) if receipt["resource_layout"] == "rank" else (7, 7)  # nccl: edge-owned slots
+    assert receipt["source_peak"] <= budget[0] and receipt["dest_peak"] <= budget[1]
 
 
 @pytest.mark.parametrize("transport", ["p2p", "nccl"])
@@ -45,4 +46,5 @@ def test_two_rank_conventional_pipeline_matches_single_gpu_bit_exact(tmp_path, t
     for b in one:
         assert torch.equal(one[b], two["outputs"][b]), b
     receipt = two["receipt"]
-    assert receipt["source_peak"] <= 2 and receipt["dest_peak"] <= 3
+    budget = (2, 3) if receipt["resource_layout"] == "rank" else (7, 7)  # nccl: edge-owned slots
+    assert receipt["source_peak"] <= budget[0] and receipt["dest_peak"] <= budget[1]
