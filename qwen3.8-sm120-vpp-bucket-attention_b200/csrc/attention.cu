@@ -197,73 +197,83 @@ QI_DEV void store_out_row(__nv_bfloat16* dst, const float* a, float norm, const 
 }
 
 // Roles.  f16 kernel (PAGED = false, 10 warps): warp 0 TMA producer, warp 1
-// TMEM allocator + MMA thread, warps 2..9 softmax.  Paged kernel (12 warps):
-// warp 0 TMEM allocator + MMA thread, warps 1..3 KV producers (warp 1's lane 0
-// also loads Q by TMA), warps 4..11 softmax.  Warp w runs on SM sub-partition
-// w % 4, so the MMA thread shares its sub-partition only with two softmax
-// warps (as in the f16 kernel), never with a producer.  384 threads at one CTA
-// per SM leave 168 registers per thread for every role.
+// TMEM allocator + MMA thread, warps 2..9 softmax.  Paged kernel (16 warps =
+// 4 warpgroups, one warp of each per SM sub-partition): warpgroup 0 the KV
+// producers (thread 0 also loads Q by TMA), warpgroups 1 and 2 the softmax of
+// the two query tiles, warp 12 the TMEM allocator + MMA thread (warps 13..15
+// idle).  The launch gives every thread 128 registers; setmaxnreg then moves
+// them to the softmax: producers 120, warpgroup 3 72, softmax 160 (per
+// sub-partition 120 + 2 x 160 + 72 = 512; per CTA 128 x 120 + 256 x 160 +
+// 128 x 72 = 65,536 = 512 x 128).  This split compiles without spills.
 template <bool PAGED>
 struct Roles {
-  static constexpr int kThreads = PAGED ? 384 : 320;
+  static constexpr int kThreads = PAGED ? 512 : 320;
   static constexpr int kSoftFirst = PAGED ? 128 : 64;  // first softmax thread
-  static constexpr int kMmaWarp = PAGED ? 0 : 1;
-  static constexpr int kProducerWarps = PAGED ? 3 : 1;
+  static constexpr int kMmaWarp = PAGED ? 12 : 1;
+  static constexpr int kProducerWarps = PAGED ? 4 : 1;
 };
 
-// Paged producer.  A key tile of K (or of V) is 128 keys x QPK = HD/32
-// quarters of 32 values; a "pass" is one warp-instruction's worth of it: KPW =
-// 32/QPK consecutive keys, lane l taking key l % KPW, quarter l / KPW
-// (consecutive lanes on consecutive keys: each quarter-warp's eight 16-byte
-// shared stores hit eight different swizzle positions, and a warp's loads
-// cover whole 64-byte key rows).  The NP = 2 x 128/KPW passes of a tile (K
-// passes first, then V) are dealt round-robin to the 3 producer warps.  A
-// tile's codes and scales are loaded into registers one tile ahead;
-// converting them writes f16 K and V into the same shared-memory tiles the
-// MMAs read: row kr of 128 bytes per 64-value half of D, 16-byte chunks
-// swizzled by kr & 7 (K-major K, MN-major V).
+// Paged producer: one thread handles QPK = HD/32 (key, 32-value quarter)
+// items of K and as many of V per key tile (mapping: paged_key / paged_quarter).  A tile's codes and scales are
+// loaded into registers one tile ahead; converting them writes f16 K and V
+// into the same shared-memory tiles the MMAs read: row kr of 128 bytes per
+// 64-value half of D, 16-byte chunks swizzled by kr & 7 (K-major K, MN-major V).
 template <int HD>
 struct PagedTile {
-  static constexpr int QPK = HD / 32, KPW = 32 / QPK, NP = 2 * 128 / KPW, MAXP = (NP + 2) / 3;
-  uint4 c[MAXP];
-  uint32_t s[MAXP];
+  static constexpr int QPK = HD / 32;
+  uint4 kc[QPK], vc[QPK];
+  uint32_t ks[QPK], vs[QPK];
 };
 
+// Item i of producer thread t: key i * (128/QPK) + (t / 32) * KPW + t % KPW,
+// quarter (t % 32) / KPW, KPW = 32/QPK keys per warp and pass.  Consecutive
+// lanes take consecutive keys, so each quarter-warp's eight 16-byte shared
+// stores land on eight different swizzle positions (no bank conflict), and a
+// warp's loads still cover whole 64-byte key rows.
 template <int HD>
-QI_DEV void paged_fetch(const AttnParams& p, int kvh, int kbase, int pw, int lane, PagedTile<HD>& b) {
-  using T = PagedTile<HD>;
-  const int qd = lane / T::KPW;
+QI_DEV int paged_key(int i, int t) {
+  constexpr int QPK = HD / 32, KPW = 32 / QPK;
+  return i * (128 / QPK) + (t >> 5) * KPW + (t & 31) % KPW;
+}
+template <int HD>
+QI_DEV int paged_quarter(int t) {
+  constexpr int KPW = 32 / (HD / 32);
+  return (t & 31) / KPW;
+}
+
+template <int HD>
+QI_DEV void paged_fetch(const AttnParams& p, int kvh, int kbase, int t, PagedTile<HD>& b) {
+  constexpr int QPK = HD / 32;
+  const int qd = paged_quarter<HD>(t);
   const int page_mask = (1 << p.page_shift) - 1;
 #pragma unroll
-  for (int k = 0; k < T::MAXP; ++k) {
-    const int pass = pw + 3 * k;
-    const bool is_v = pass >= T::NP / 2;
-    const int token = kbase + (pass % (T::NP / 2)) * T::KPW + lane % T::KPW;
-    if (pass < T::NP && token < p.kv_tokens) {
+  for (int i = 0; i < QPK; ++i) {
+    const int token = kbase + paged_key<HD>(i, t);
+    if (token < p.kv_tokens) {
       const int64_t page = __ldg(p.block_table + (token >> p.page_shift)), entry = token & page_mask;
       const int64_t dofs = page * p.data_page + entry * p.data_row + (int64_t)kvh * p.data_head + qd * 16;
       const int64_t sofs = page * p.sf_page + entry * p.sf_row + (int64_t)kvh * p.sf_head + qd * 2;
-      b.c[k] = __ldg(reinterpret_cast<const uint4*>((is_v ? p.vc : p.kc) + dofs));
-      b.s[k] = __ldg(reinterpret_cast<const unsigned short*>((is_v ? p.vsf : p.ksf) + sofs));
+      b.kc[i] = __ldg(reinterpret_cast<const uint4*>(p.kc + dofs));
+      b.vc[i] = __ldg(reinterpret_cast<const uint4*>(p.vc + dofs));
+      b.ks[i] = __ldg(reinterpret_cast<const unsigned short*>(p.ksf + sofs));
+      b.vs[i] = __ldg(reinterpret_cast<const unsigned short*>(p.vsf + sofs));
     } else {
-      b.c[k] = make_uint4(0, 0, 0, 0);
-      b.s[k] = 0;
+      b.kc[i] = b.vc[i] = make_uint4(0, 0, 0, 0);
+      b.ks[i] = b.vs[i] = 0;
     }
   }
 }
 
-// e2m1 x e4m3 -> f16 (exact) of this warp's K (want_v = false) or V passes.
+// e2m1 x e4m3 -> f16 (exact) into a [D/64][128 keys][128 B] swizzled tile.
 template <int HD>
-QI_DEV void paged_put(const PagedTile<HD>& b, uint8_t* tile, int pw, int lane, bool want_v) {
-  using T = PagedTile<HD>;
-  const int qd = lane / T::KPW;
+QI_DEV void paged_put(const uint4* codes, const uint32_t* scales, uint8_t* tile, int t) {
+  constexpr int QPK = HD / 32;
+  const int qd = paged_quarter<HD>(t);
 #pragma unroll
-  for (int k = 0; k < T::MAXP; ++k) {
-    const int pass = pw + 3 * k;
-    if (pass >= T::NP || (pass >= T::NP / 2) != want_v) continue;  // warp-uniform
-    const int kr = (pass % (T::NP / 2)) * T::KPW + lane % T::KPW;
-    const uint32_t s2 = e4m3x2_to_f16x2(b.s[k] & 0xFFFFu);
-    const uint32_t words[4] = {b.c[k].x, b.c[k].y, b.c[k].z, b.c[k].w};
+  for (int i = 0; i < QPK; ++i) {
+    const int kr = paged_key<HD>(i, t);
+    const uint32_t s2 = e4m3x2_to_f16x2(scales[i] & 0xFFFFu);
+    const uint32_t words[4] = {codes[i].x, codes[i].y, codes[i].z, codes[i].w};
     uint8_t* row = tile + (qd >> 1) * (128 * 128) + kr * 128;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {  // 16-byte output chunk c: elements 8c .. 8c+7 of the quarter
@@ -623,15 +633,14 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads, 1)
     }
   };
   if constexpr (PAGED) {
-    if (warp == R::kMmaWarp) {
-      mma_role();
-    } else if (warp <= R::kProducerWarps) {
-      const int pw = warp - 1;  // producer warp 0 .. 2
-      if (pw == 0 && lane == 0) {
+    if (warp < 4) {
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 120;");
+      const int t = threadIdx.x;  // 0 .. 127
+      if (t == 0) {
         mbar_expect_tx(q_full, NQ * Q_TILE);
-#pragma unroll
+  #pragma unroll
         for (int qt = 0; qt < NQ; ++qt)
-#pragma unroll
+  #pragma unroll
           for (int a = 0; a < HD / 64; ++a)
             tma_load_2d(sQ + qt * Q_TILE + a * ATOM, &tq, q_full, head * HD + 64 * a, q0 + qt * TQ);
       }
@@ -639,43 +648,47 @@ __global__ void __launch_bounds__(Roles<PAGED>::kThreads, 1)
       // done, convert, make the generic-proxy writes visible to the tensor
       // cores, then one arrival per warp.  Tile j + 1 is loaded first.
       auto step = [&](PagedTile<HD>& cur, PagedTile<HD>& nxt, int j) -> bool {
-        if (j + 1 < ntiles) paged_fetch<HD>(p, kvh, (j_first + j + 1) * TK, pw, lane, nxt);
+        if (j + 1 < ntiles) paged_fetch<HD>(p, kvh, (j_first + j + 1) * TK, t, nxt);
         const int s = j & 1;
         if (j >= 2 && !mbar_wait(&k_empty[s], ((j >> 1) - 1) & 1, abort_flag, p.status)) return false;
-        paged_put<HD>(cur, sK + s * K_BYTES, pw, lane, false);
+        paged_put<HD>(cur.kc, cur.ks, sK + s * K_BYTES, t);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&k_full[s]);
         if (j >= 2 && !mbar_wait(&v_empty[s], ((j >> 1) - 1) & 1, abort_flag, p.status)) return false;
-        paged_put<HD>(cur, sV + s * V_BYTES, pw, lane, true);
+        paged_put<HD>(cur.vc, cur.vs, sV + s * V_BYTES, t);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&v_full[s]);
         return true;
       };
       PagedTile<HD> ta, tb;
-      if (ntiles > 0) paged_fetch<HD>(p, kvh, j_first * TK, pw, lane, ta);
+      if (ntiles > 0) paged_fetch<HD>(p, kvh, j_first * TK, t, ta);
       for (int j = 0; j < ntiles; j += 2) {
         if (!step(ta, tb, j)) break;
         if (j + 1 < ntiles && !step(tb, ta, j + 1)) break;
       }
+    } else if (warp >= 12) {
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 72;");
+      if (warp == 12) mma_role();  // warps 13..15 only take part in the CTA barriers
     } else {
+      asm volatile("setmaxnreg.inc.sync.aligned.u32 160;");
       softmax_role();
     }
   } else {
     if (warp == 0) {
       if (lane == 0) {
         mbar_expect_tx(q_full, NQ * Q_TILE);
-#pragma unroll
+  #pragma unroll
         for (int t = 0; t < NQ; ++t)
-#pragma unroll
+  #pragma unroll
           for (int a = 0; a < HD / 64; ++a)
             tma_load_2d(sQ + t * Q_TILE + a * ATOM, &tq, q_full, head * HD + 64 * a, q0 + t * TQ);
         for (int j = 0; j < ntiles; ++j) {
           const int s = j & 1;
           if (j >= 2 && !mbar_wait(&k_empty[s], ((j >> 1) - 1) & 1, abort_flag, p.status)) break;
           mbar_expect_tx(&k_full[s], K_BYTES);
-#pragma unroll
+  #pragma unroll
           for (int a = 0; a < HD / 64; ++a)
             tma_load_3d(sK + s * K_BYTES + a * ATOM, &tk, &k_full[s], 64 * a, (j_first + j) * TK, kvh);
           if (j >= 2 && !mbar_wait(&v_empty[s], ((j >> 1) - 1) & 1, abort_flag, p.status)) break;
