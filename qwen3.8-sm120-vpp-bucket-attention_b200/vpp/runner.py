@@ -70,12 +70,11 @@ class FoldedRank:
         # of each other at any moment (the first traversal's stage on chunk
         # j + k beside the second traversal's on chunk j), so they run on two
         # CUDA streams and each one's kernels fill the SMs the other leaves
-        # idle (partial last waves, small producers).  Default: on for the fold
-        # on one GPU or over the peer-to-peer transport (whose boundary waits
-        # are events on the consuming stream); the NCCL comparison transport
-        # keeps the single stream.
-        p2p = transport is not None and getattr(transport, "backend", None) == "p2p"
-        can = profile == "vpp" and (ranks == 1 or p2p) and self.device.type == "cuda"
+        # idle (partial last waves, small producers).  Default: on for the fold,
+        # on one GPU and over either transport: boundary waits are stream waits
+        # on the consuming stage's stream (the peer copy's event, or the
+        # grouped NCCL receive of the edge's own communicator).
+        can = profile == "vpp" and self.device.type == "cuda"
         self.overlap = can if overlap is None else (bool(overlap) and can)
         self.model = StageModel(shape, layers, self.device, max_rows=chunk, request_tokens=self.request_tokens,
                                 base_seed=base_seed, on_device_init=on_device_init,

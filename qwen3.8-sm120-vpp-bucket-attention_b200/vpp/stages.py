@@ -21,9 +21,12 @@ grants destination slots strictly in the order it will consume its inputs (so
 the input it needs next always holds a slot) and makes its compute stream wait
 on the sender's event.
 
-``backend="nccl"``: the comparison transport — the same slots, with
-``isend``/``irecv`` of the two planes on one NCCL group per traversal
-direction (the reference's ``--transport nccl``, ``vpp/worker.py:86-110``).
+``backend="nccl"``: the comparison transport (the reference's ``NcclEdge``,
+``vpp/native/nccl_edge.cpp:30-107``): one 2-rank NCCL communicator per wire
+edge, both planes of a message as one grouped send / receive
+(``batch_isend_irecv``), edge-owned slots.  Each edge is used by one stage on
+each side, so a rank's two stages may run on two CUDA streams with either
+transport.
 
 Every host wait has a deadline (``timeout``, default 60 s); a failure flags the
 edge's control page so the peer's waits end too.
@@ -235,7 +238,14 @@ class StageBoundaries:
 
     def _setup_nccl(self):
         self.session = None
-        self.nccl_groups = (dist.new_group(backend="nccl"), dist.new_group(backend="nccl"))
+        # every rank creates every edge's group, in edge order (group creation
+        # is collective); a rank uses the groups of its own edges only
+        self.edge_groups = {}
+        for src in range(2 * self.ranks - 1):
+            if L.stage_rank(src, self.ranks) == L.stage_rank(src + 1, self.ranks):
+                continue  # the local fold
+            e = _Edge(src, self.ranks)
+            self.edge_groups[src] = dist.new_group(ranks=sorted((e.src_rank, e.dst_rank)), backend="nccl")
         self.dst_arena = torch.empty((self.n_dst, 2, self.capacity, self.hidden), dtype=torch.bfloat16,
                                      device=self.device)
         self.nccl_sends = {}  # physical source slot -> works
@@ -386,10 +396,10 @@ class StageBoundaries:
                 self.ipc_out[stage][seq % 8], self.src_done[p].cuda_event), "peer copy")
             self.ctrl_out[stage].publish(seq, self.layout.encode(d))
         else:
-            grp = self.nccl_groups[0 if e.forward else 1]
-            works = [dist.isend(self.src_arena[p, 0, :rows], dst=e.dst_rank, group=grp),
-                     dist.isend(self.src_arena[p, 1, :rows], dst=e.dst_rank, group=grp)]
-            self.nccl_sends[p] = works
+            grp = self.edge_groups[e.src_stage]
+            self.nccl_sends[p] = dist.batch_isend_irecv(
+                [dist.P2POp(dist.isend, self.src_arena[p, 0, :rows], e.dst_rank, group=grp),
+                 dist.P2POp(dist.isend, self.src_arena[p, 1, :rows], e.dst_rank, group=grp)])
         self.res_marked[p] = False
         ring.transition(ticket, NV.OP_TRANSFER_RECORDED)
         self.src_busy[p] = (stage, ticket)
@@ -433,11 +443,11 @@ class StageBoundaries:
             p = self.dst_leases.take(stage, ticket)
             self.dst_busy[p] = (stage, ticket)
             e = self.in_edges[stage]
-            grp = self.nccl_groups[0 if e.forward else 1]
-            w1 = dist.irecv(self.dst_arena[p, 0, :rows], src=e.src_rank, group=grp)
-            w2 = dist.irecv(self.dst_arena[p, 1, :rows], src=e.src_rank, group=grp)
-            w1.wait()
-            w2.wait()
+            grp = self.edge_groups[e.src_stage]
+            for w in dist.batch_isend_irecv(
+                    [dist.P2POp(dist.irecv, self.dst_arena[p, 0, :rows], e.src_rank, group=grp),
+                     dist.P2POp(dist.irecv, self.dst_arena[p, 1, :rows], e.src_rank, group=grp)]):
+                w.wait()  # the current (consuming) stream waits; the host does not block
         ring = self.dst_rings[stage]
         ring.transition(ticket, NV.OP_TRANSFER_RECORDED)
         ring.transition(ticket, NV.OP_CONSUMER_RECORDED)
