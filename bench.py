@@ -69,9 +69,10 @@ def parse():
     p.add_argument("--layers", type=int, default=None, help="override layer count (must split into 2N stages)")
     p.add_argument("--overlap", choices=("auto", "on", "off"), default="auto",
                    help="one GPU: run the two virtual stages on two CUDA streams (auto: on for N=1)")
-    p.add_argument("--attention", choices=("paged", "f16"), default="paged",
-                   help="paged: attention reads the NVFP4 cache directly (default); f16: the two-step comparison "
-                        "path (dequantise to f16 K/V^T, then attention)")
+    p.add_argument("--attention", choices=("auto", "paged", "f16"), default="auto",
+                   help="paged: attention reads the NVFP4 cache directly; f16: dequantise each chunk's new keys "
+                        "into an f16 K/V^T copy kept per request, then the TMA-fed kernel; auto (default): f16 "
+                        "when the copies fit in memory, else paged")
     p.add_argument("--kv-shadow", choices=("auto", "on", "off"), default="auto",
                    help="--attention f16 only: keep each request's f16 K/V^T across its chunks")
     p.add_argument("--workload", choices=("prefill", "decode", "producers"), default="prefill",
@@ -466,7 +467,7 @@ def run_ours(args):
                     prompt_tokens=reqs, chunk=args.chunk_size,
                     virtual_stages=2 * world if args.profile == "vpp" else world,
                     parallelism=f"folded-vpp pp{world}" if args.profile == "vpp" else f"pp{world}", transport=(args.transport if world > 1 else "local fold"),
-                    stage_streams=2 if runner.overlap else 1, attention=args.attention,
+                    stage_streams=2 if runner.overlap else 1, attention=runner.model.attention,
                     l2="inputs larger than L2 (weights ~16 GB, KV pages)"),
         bubble_fraction=bubble, busiest_rank_compute_ms=busiest, instrumented_bank_ms=makespan,
         model_tflops=total_flops / (ms / 1e3) / 1e12,

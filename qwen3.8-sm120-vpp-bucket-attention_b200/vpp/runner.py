@@ -48,7 +48,7 @@ class FoldedRank:
 
     def __init__(self, shape, rank, ranks, device, request_tokens, chunk, *, transport=None, base_seed=1234,
                  on_device_init=None, keep_all_outputs=False, profile="vpp", kv_shadow=None, overlap=None,
-                 attention="paged"):
+                 attention="auto"):
         if profile not in L.PROFILES:
             raise ValueError("profile is vpp or cpp")
         self.shape, self.rank, self.ranks, self.profile = shape, rank, ranks, profile
