@@ -35,6 +35,7 @@ edge's control page so the peer's waits end too.
 import os
 import time
 import uuid
+from datetime import timedelta
 
 import torch
 import torch.distributed as dist
@@ -245,7 +246,8 @@ class StageBoundaries:
             if L.stage_rank(src, self.ranks) == L.stage_rank(src + 1, self.ranks):
                 continue  # the local fold
             e = _Edge(src, self.ranks)
-            self.edge_groups[src] = dist.new_group(ranks=sorted((e.src_rank, e.dst_rank)), backend="nccl")
+            self.edge_groups[src] = dist.new_group(ranks=sorted((e.src_rank, e.dst_rank)), backend="nccl",
+                                                   timeout=timedelta(seconds=self.timeout))
         self.dst_arena = torch.empty((self.n_dst, 2, self.capacity, self.hidden), dtype=torch.bfloat16,
                                      device=self.device)
         self.nccl_sends = {}  # physical source slot -> works

@@ -13,10 +13,11 @@ copies, slot wrap-around (7-slot rings, 2 source / 3 destination physical
 slots) and the final drain.
 
 ``timed=True`` instead sends full-capacity messages and measures, with CUDA
-events on the sending rank's copy stream, the bytes copied per second over
-NVLink (both planes: 2 x C x H x 2 bytes per message).
+events on the sending rank's copy stream, the bytes moved per second
+through the whole protocol (credit waits included).  ``copy_rate`` times the
+boundary copy alone (``--copy-rate [--both]``).
 
-    python -m qwen_infra_b200.vpp.stress --gpus 2 [--backend p2p|nccl] [--timed]
+    python -m qwen_infra_b200.vpp.stress --gpus 2 [--backend p2p|nccl] [--timed | --copy-rate [--both]]
 
 One process per GPU (spawned here), NCCL process group, gloo control plane.
 """
@@ -109,6 +110,52 @@ def run_rank(rank, world, device, *, capacity, hidden, messages, backend="p2p", 
     return receipt
 
 
+def copy_rate(rank, world, device, *, capacity=2048, hidden=5120, reps=50, both=False, segment=16 << 20):
+    """NVLink rate of the transport's boundary copy itself (qv_copy_message:
+    both planes of a C x H bf16 message, peer to peer into an IPC-mapped
+    destination), without the credit protocol: rank 0 (and with ``both`` also
+    rank 1, to rank 0 at the same time) copies ``reps`` messages back to back
+    on one stream, timed with CUDA events on that stream."""
+    from . import native as NV
+
+    plane = capacity * hidden * 2
+    dst_ptr, handle = NV.arena_alloc(device.index, 2 * plane)
+    handles = [None] * world
+    dist.all_gather_object(handles, handle)
+    src = torch.empty(2 * plane, dtype=torch.uint8, device=device)
+    src.fill_(rank + 1)
+    torch.cuda.synchronize(device)
+    result = dict(rank=rank, capacity=capacity, hidden=hidden, message_bytes=2 * plane, reps=reps, both=both)
+    sending = rank == 0 or (both and rank == 1)
+    peer = 1 - rank
+    peer_ptr = NV.arena_open(device.index, handles[peer]) if sending else None
+    dist.barrier()
+    if sending:
+        stream = torch.cuda.Stream(device=device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+        def issue():
+            NV.cuda_check(NV.lib().qv_copy_message(device.index, stream.cuda_stream, None, None, src.data_ptr(),
+                                                   src.data_ptr() + plane, peer_ptr, peer_ptr + plane, plane,
+                                                   segment, None, None), "peer copy")
+
+        for _ in range(3):
+            issue()
+        e0.record(stream)
+        for _ in range(reps):
+            issue()
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1)
+        result.update(ms=ms, gbs=reps * 2 * plane / (ms / 1e3) / 1e9, us_per_message=ms * 1e3 / reps)
+    dist.barrier()
+    if sending:
+        NV.lib().qv_arena_close(device.index, peer_ptr)
+    dist.barrier()
+    NV.lib().qv_arena_free(device.index, dst_ptr)
+    return result
+
+
 def _worker(rank, world, port, kwargs, out_dir):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
@@ -117,7 +164,9 @@ def _worker(rank, world, port, kwargs, out_dir):
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                             timeout=timedelta(seconds=kwargs.get("timeout", 60.0) + 30))
     try:
-        receipt = run_rank(rank, world, dev, **kwargs)
+        kwargs = dict(kwargs)
+        mode = kwargs.pop("mode", "walk")
+        receipt = (copy_rate if mode == "copy" else run_rank)(rank, world, dev, **kwargs)
         Path(out_dir, f"rank{rank}.json").write_text(json.dumps(receipt))
     finally:
         dist.destroy_process_group()
@@ -159,9 +208,15 @@ def main(argv=None):
     ap.add_argument("--backend", choices=("p2p", "nccl"), default="p2p")
     ap.add_argument("--resource-layout", choices=("rank", "edge"), default=None)
     ap.add_argument("--timed", action="store_true")
+    ap.add_argument("--copy-rate", action="store_true",
+                    help="time back-to-back boundary copies (no credit protocol) instead of the walk")
+    ap.add_argument("--both", action="store_true", help="--copy-rate: both directions at once")
     a = ap.parse_args(argv)
-    receipts = launch(a.gpus, capacity=a.capacity, hidden=a.hidden, messages=a.messages, backend=a.backend,
-                      resource_layout=a.resource_layout, timed=a.timed)
+    if a.copy_rate:
+        receipts = launch(a.gpus, mode="copy", capacity=a.capacity, hidden=a.hidden, both=a.both)
+    else:
+        receipts = launch(a.gpus, capacity=a.capacity, hidden=a.hidden, messages=a.messages, backend=a.backend,
+                          resource_layout=a.resource_layout, timed=a.timed)
     for r in receipts:
         print(json.dumps(r))
     return 0
