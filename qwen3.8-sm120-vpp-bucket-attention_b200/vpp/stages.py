@@ -351,13 +351,15 @@ class StageBoundaries:
         seq = self.out_seq[stage]
         d = self.layout.make(self.epoch, batch, seq, stage, rows)
         ring = self.src_rings[stage]
-        ticket = ring.try_acquire(d)
-        if ticket is None:
-            raise NV.BoundaryError("source ring slot still busy")
+        # Wait for the physical slot first: with edge-owned slots it is the
+        # ring slot itself, which the message seq - 7 may still hold.
         if not self.src_leases.can_take(stage, seq):
             self.src_leases.note_stall()
             self.stats["slot_waits"] += 1
             self._deadline_loop("a free source slot", lambda: self.src_leases.can_take(stage, seq))
+        ticket = ring.try_acquire(d)
+        if ticket is None:
+            raise NV.BoundaryError("source ring slot still busy")
         p = self.src_leases.take(stage, ticket)
         self.src_busy[p] = None
         self.src_current[(batch, stage)] = (p, ticket, d)

@@ -125,7 +125,8 @@ def copy_rate(rank, world, device, *, capacity=2048, hidden=5120, reps=50, both=
     src = torch.empty(2 * plane, dtype=torch.uint8, device=device)
     src.fill_(rank + 1)
     torch.cuda.synchronize(device)
-    result = dict(rank=rank, capacity=capacity, hidden=hidden, message_bytes=2 * plane, reps=reps, both=both)
+    result = dict(rank=rank, capacity=capacity, hidden=hidden, message_bytes=2 * plane, reps=reps, both=both,
+                  segment=segment)
     sending = rank == 0 or (both and rank == 1)
     peer = 1 - rank
     peer_ptr = NV.arena_open(device.index, handles[peer]) if sending else None
@@ -211,9 +212,10 @@ def main(argv=None):
     ap.add_argument("--copy-rate", action="store_true",
                     help="time back-to-back boundary copies (no credit protocol) instead of the walk")
     ap.add_argument("--both", action="store_true", help="--copy-rate: both directions at once")
+    ap.add_argument("--segment", type=int, default=16 << 20, help="--copy-rate: bytes per cudaMemcpyAsync (0: whole plane)")
     a = ap.parse_args(argv)
     if a.copy_rate:
-        receipts = launch(a.gpus, mode="copy", capacity=a.capacity, hidden=a.hidden, both=a.both)
+        receipts = launch(a.gpus, mode="copy", capacity=a.capacity, hidden=a.hidden, both=a.both, segment=a.segment)
     else:
         receipts = launch(a.gpus, capacity=a.capacity, hidden=a.hidden, messages=a.messages, backend=a.backend,
                           resource_layout=a.resource_layout, timed=a.timed)

@@ -119,3 +119,28 @@ def test_resource_layout_rules():
         StageBoundaries(0, 2, "cpu", 64, 256, backend="nccl", resource_layout="rank")
     with pytest.raises(ValueError):
         StageBoundaries(0, 2, "cpu", 64, 256, resource_layout="ring")
+
+
+def test_edge_layout_sender_waits_for_its_ring_slot():
+    """A sender 7 messages ahead on edge-owned slots must wait for slot
+    seq % 7 to come back (it is the ring slot itself), not fail."""
+    t = _bare(timeout=0.2)
+    t.out_edges = {0: None}
+    t.src_leases = ST._EdgeSlots(2, t.out_edges)
+    t.layout = NV.BoundaryLayout(64, 7, 2, 256)
+    t.epoch, t.capacity = 1, 64
+    t.src_rings = {0: NV.SlotRing(NV.SOURCE, t.layout, 1, 0)}
+    t.out_seq = {0: 0}
+    t.src_busy = [None] * 7
+    t.src_current = {}
+    t.stats = dict(slot_waits=0)
+    t.src_arena = __import__("torch").zeros((7, 2, 64, 256))
+    reaped = []
+    t._reap = lambda: reaped.append(1)
+    t.closed = t.failed = False
+    for seq in range(7):
+        t.prepare_send(seq, 0, 8)
+        t.out_seq[0] += 1
+    with pytest.raises(NV.TransportTimeout):  # slot 0 still held: a bounded wait, then the deadline
+        t.prepare_send(7, 0, 8)
+    assert reaped and t.stats["slot_waits"] == 1
