@@ -142,7 +142,7 @@ def boundary_edges(rank, ranks, profile="vpp"):
 
 class StageBoundaries:
     def __init__(self, rank, ranks, device, capacity, hidden, *, backend="p2p", epoch=1, timeout=60.0,
-                 segment_bytes=16 << 20, control_group=None, session=None, profile="vpp", resource_layout=None):
+                 segment_bytes=0, control_group=None, session=None, profile="vpp", resource_layout=None):
         if ranks < 2:
             raise ValueError("a boundary transport needs at least two ranks")
         if backend not in ("p2p", "nccl"):

@@ -110,7 +110,7 @@ def run_rank(rank, world, device, *, capacity, hidden, messages, backend="p2p", 
     return receipt
 
 
-def copy_rate(rank, world, device, *, capacity=2048, hidden=5120, reps=50, both=False, segment=16 << 20):
+def copy_rate(rank, world, device, *, capacity=2048, hidden=5120, reps=50, both=False, segment=0):
     """NVLink rate of the transport's boundary copy itself (qv_copy_message:
     both planes of a C x H bf16 message, peer to peer into an IPC-mapped
     destination), without the credit protocol: rank 0 (and with ``both`` also
@@ -212,7 +212,7 @@ def main(argv=None):
     ap.add_argument("--copy-rate", action="store_true",
                     help="time back-to-back boundary copies (no credit protocol) instead of the walk")
     ap.add_argument("--both", action="store_true", help="--copy-rate: both directions at once")
-    ap.add_argument("--segment", type=int, default=16 << 20, help="--copy-rate: bytes per cudaMemcpyAsync (0: whole plane)")
+    ap.add_argument("--segment", type=int, default=0, help="--copy-rate: bytes per cudaMemcpyAsync (0: whole plane)")
     a = ap.parse_args(argv)
     if a.copy_rate:
         receipts = launch(a.gpus, mode="copy", capacity=a.capacity, hidden=a.hidden, both=a.both, segment=a.segment)
