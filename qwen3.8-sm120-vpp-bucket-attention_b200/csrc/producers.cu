@@ -366,10 +366,28 @@ __global__ void gate_fp8_kernel(const __nv_bfloat16* __restrict__ out, const __n
   }
   if (!active) return;
   uint32_t w[4];
+  if (static_scale) {
 #pragma unroll
-  for (int k = 0; k < 4; ++k)
-    w[k] = f2_to_e4m3x2(__fdiv_rn(v[4 * k], scale), __fdiv_rn(v[4 * k + 1], scale)) |
-           (f2_to_e4m3x2(__fdiv_rn(v[4 * k + 2], scale), __fdiv_rn(v[4 * k + 3], scale)) << 16);
+    for (int k = 0; k < 4; ++k)
+      w[k] = f2_to_e4m3x2(__fdiv_rn(v[4 * k], scale), __fdiv_rn(v[4 * k + 1], scale)) |
+             (f2_to_e4m3x2(__fdiv_rn(v[4 * k + 2], scale), __fdiv_rn(v[4 * k + 3], scale)) << 16);
+  } else {
+    // v / scale correctly rounded from one reciprocal per row, by Markstein's
+    // correction step (IBM J. Res. Dev. 34(1), 1990): y = RN(1/s),
+    // q = RN(v y), r = v - s q (exact with an FMA), RN(q + r y) = RN(v / s)
+    // whenever the quotient is a normal number.  Here |v| <= 448 s, so it
+    // never overflows; a quotient below the normal range encodes to e4m3
+    // zero either way.
+    const float y = __frcp_rn(scale);
+    auto quot = [&](float a) {
+      const float q0 = __fmul_rn(a, y);
+      return __fmaf_rn(__fmaf_rn(-q0, scale, a), y, q0);
+    };
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      w[k] = f2_to_e4m3x2(quot(v[4 * k]), quot(v[4 * k + 1])) |
+             (f2_to_e4m3x2(quot(v[4 * k + 2]), quot(v[4 * k + 3])) << 16);
+  }
   reinterpret_cast<uint4*>(fp8 + row * fp8_row)[t] = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
