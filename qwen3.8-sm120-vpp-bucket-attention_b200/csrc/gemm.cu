@@ -304,14 +304,23 @@ __global__ void __launch_bounds__(THREADS, 1)
 // the MMAs (measured: 4 NVFP4 MMAs of a K tile 513 clk alone, 946 clk with the
 // 12 copies that feed them).  Here four warps write the scales into TMEM with
 // tcgen05.st instead (the same replicated 4 x 32-lane layout the copies
-// produce), through their own 4-stage TMEM ring, and the MMAs run without
-// interruption.  16 warps, registers rebalanced with setmaxnreg:
-//   warps 0..3   (56 regs): warp 0 TMA producer, warp 1 TMEM allocator + MMA issuer,
+// produce), through their own TMEM ring, and the MMAs run without
+// interruption.  The scales have their own shared-memory ring and producer
+// thread too, one stage deeper than the A/B ring: the scale writers used to
+// start only when a stage's A/B data had landed, and their latency came on
+// top of it (a clock trace of the MMA thread: 2961 of 18898 clk per QKV tile
+// spent waiting for scales).  16 warps, registers rebalanced with setmaxnreg:
+//   warps 0..3   (56 regs): warp 0 A/B TMA producer, warp 1 TMEM allocator +
+//                           MMA issuer, warp 2 scale producer,
 //   warps 4..7   (72 regs): scale writers, one per TMEM lane quarter,
 //   warps 8..15 (192 regs): epilogue, two warps per lane quarter.
 
 constexpr int S_THREADS = 512;
-constexpr int NSF = 4;                 // TMEM scale stages
+constexpr int S_SST = 5;               // shared-memory scale stages
+constexpr int NSF = 5;                 // TMEM scale stages
+constexpr int S_SMEM = STAGES * (A_BYTES + B_BYTES) + S_SST * (SFA_BYTES + SFB_BYTES) + 1024 /*align*/ +
+                       256 /*barriers*/;
+static_assert(S_SMEM + 64 <= 227 * 1024, "scale-writer GEMM exceeds shared memory");
 constexpr uint32_t S_SF_COL = 256;     // stage t: columns S_SF_COL + 48t .. +48
 constexpr int S_SF_STAGE_COLS = 48;    // 16 for A (4 MMAs x 4), 32 for B (4 MMAs x 2 halves x 4)
 static_assert(S_SF_COL + NSF * S_SF_STAGE_COLS <= TMEM_COLS, "scale stages exceed TMEM");
@@ -333,12 +342,14 @@ __global__ void __launch_bounds__(S_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + STAGES * A_BYTES;
-  uint8_t* sSFA = sB + STAGES * B_BYTES;
-  uint8_t* sSFB = sSFA + STAGES * SFA_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sSFB + STAGES * SFB_BYTES);
+  uint8_t* sSFA = sB + STAGES * B_BYTES;   // [S_SST]
+  uint8_t* sSFB = sSFA + S_SST * SFA_BYTES;  // [S_SST]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sSFB + S_SST * SFB_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* sf_full = empty + STAGES;  // [NSF]
-  uint64_t* sf_empty = sf_full + NSF;  // [NSF]
+  uint64_t* sc_full = empty + STAGES;     // [S_SST] scales in shared memory
+  uint64_t* sc_empty = sc_full + S_SST;   // [S_SST]
+  uint64_t* sf_full = sc_empty + S_SST;   // [NSF] scales in TMEM
+  uint64_t* sf_empty = sf_full + NSF;     // [NSF]
   uint64_t* acc_full = sf_empty + NSF;
   uint64_t* acc_empty = acc_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
@@ -353,6 +364,10 @@ __global__ void __launch_bounds__(S_THREADS, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < S_SST; ++s) {
+      mbar_init(&sc_full[s], 1);
+      mbar_init(&sc_empty[s], 4);  // one arrival per scale-writer warp
     }
     for (int t = 0; t < NSF; ++t) {
       mbar_init(&sf_full[t], 4);  // one arrival per scale-writer warp
@@ -372,7 +387,7 @@ __global__ void __launch_bounds__(S_THREADS, 1)
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
     if (warp == 0 && lane == 0) {
-      constexpr uint32_t tx = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+      constexpr uint32_t tx = A_BYTES + B_BYTES;
       uint32_t it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
@@ -383,12 +398,25 @@ __global__ void __launch_bounds__(S_THREADS, 1)
           mbar_expect_tx(&full[s], tx);
           tma_load_2d(sA + s * A_BYTES, &tma_a, &full[s], kt * BKB, m0);
           tma_load_2d(sB + s * B_BYTES, &tma_b, &full[s], kt * BKB, n0);
+        }
+      }
+    } else if (warp == 2 && lane == 0) {
+      // Scale producer: each K tile's A and B block scales (6 KB) into the
+      // scale ring, as far ahead as the scale writers free its stages.
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+        const int m0 = (tile % p.m_tiles) * BM, n0 = (tile / p.m_tiles) * BN;
+        for (int kt = 0; kt < p.kt; ++kt, ++it) {
+          const int s = it % S_SST;
+          if (it >= S_SST && !(ok = mbar_wait(&sc_empty[s], ((it / S_SST) - 1) & 1, abort_flag, p.status))) break;
+          mbar_expect_tx(&sc_full[s], SFA_BYTES + SFB_BYTES);
           bulk_load(sSFA + s * SFA_BYTES, p.sfa + (int64_t)(m0 >> 7) * p.sfa_block + (int64_t)kt * 2048, 2048,
-                    &full[s]);
+                    &sc_full[s]);
           bulk_load(sSFB + s * SFB_BYTES, p.sfb + (int64_t)(n0 >> 7) * p.sfb_block + (int64_t)kt * 2048, 2048,
-                    &full[s]);
+                    &sc_full[s]);
           bulk_load(sSFB + s * SFB_BYTES + 2048, p.sfb + (int64_t)((n0 >> 7) + 1) * p.sfb_block + (int64_t)kt * 2048,
-                    2048, &full[s]);
+                    2048, &sc_full[s]);
         }
       }
     } else if (warp == 1 && lane == 0) {
@@ -427,8 +455,8 @@ __global__ void __launch_bounds__(S_THREADS, 1)
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
       for (int kt = 0; kt < p.kt; ++kt, ++it) {
-        const int s = it % STAGES, t = it % NSF;
-        if (!(ok = mbar_wait(&full[s], (it / STAGES) & 1, abort_flag, p.status))) break;
+        const int s = it % S_SST, t = it % NSF;
+        if (!(ok = mbar_wait(&sc_full[s], (it / S_SST) & 1, abort_flag, p.status))) break;
         if (it >= NSF && !(ok = mbar_wait(&sf_empty[t], ((it / NSF) - 1) & 1, abort_flag, p.status))) break;
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
@@ -450,7 +478,10 @@ __global__ void __launch_bounds__(S_THREADS, 1)
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sf_full[t]);
+        if (lane == 0) {
+          mbar_arrive(&sf_full[t]);
+          mbar_arrive(&sc_empty[s]);  // the shared-memory stage was read into registers above
+        }
       }
     }
   } else {
@@ -759,7 +790,7 @@ int launch_sfw(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, cu
   if (cur_dev < 0 || cur_dev >= 64) return (int)cudaErrorInvalidDevice;
   if (!configured[cur_dev]) {
     cudaError_t e = cudaFuncSetAttribute(gemm_sfw_kernel<kEpi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         SMEM_BYTES + 64);
+                                         S_SMEM + 64);
     if (e != cudaSuccess) return (int)e;
     e = cudaDeviceGetAttribute(&sms[cur_dev], cudaDevAttrMultiProcessorCount, cur_dev);
     if (e != cudaSuccess) return (int)e;
@@ -767,7 +798,7 @@ int launch_sfw(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, cu
   }
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = tiles < sms[cur_dev] ? tiles : sms[cur_dev];
-  gemm_sfw_kernel<kEpi><<<grid, S_THREADS, SMEM_BYTES + 64, stream>>>(ma, mb, p);
+  gemm_sfw_kernel<kEpi><<<grid, S_THREADS, S_SMEM + 64, stream>>>(ma, mb, p);
   return (int)cudaPeekAtLastError();
 }
 
@@ -895,7 +926,7 @@ int qi_gemm_resources(int* out) {
   cudaFuncAttributes a{};
   const cudaError_t e = cudaFuncGetAttributes(&a, gemm_sfw_kernel<QI_EPI_BF16>);
   if (e != cudaSuccess) return (int)e;
-  out[0] = SMEM_BYTES + 64;
+  out[0] = S_SMEM + 64;
   out[1] = a.numRegs;
   out[2] = S_THREADS;
   return 0;
