@@ -57,7 +57,9 @@ def parse():
     p.add_argument("--prompt-tokens", default="32768",
                    help="tokens per request, or a comma-separated list (one request each)")
     p.add_argument("--chunk-size", type=int, default=2048)
-    p.add_argument("--transport", choices=("p2p", "nccl"), default="p2p")
+    p.add_argument("--transport", type=_transports, default=["p2p"],
+                   help="p2p | nccl | p2p,nccl (the second is timed on the same bank after the first, "
+                        "with N > 1, and reported under transport_compare)")
     p.add_argument("--resource-layout", choices=("rank", "edge"), default=None,
                    help="boundary slots: rank-shared 2+3 (p2p default) or 7 per edge endpoint (nccl default)")
     p.add_argument("--profile", choices=("vpp", "cpp"), default="vpp",
@@ -271,6 +273,13 @@ def run_reference(args):
     return 0
 
 
+def _transports(text):
+    names = [t.strip() for t in text.split(",") if t.strip()]
+    if not names or len(names) > 2 or len(set(names)) != len(names) or any(n not in ("p2p", "nccl") for n in names):
+        raise argparse.ArgumentTypeError("expected p2p, nccl or p2p,nccl")
+    return names
+
+
 def _workload(args, reqs):
     lens = f"{len(reqs)}x{reqs[0]}" if len(set(reqs)) == 1 else "+".join(str(t) for t in reqs)
     return f"{args.model} {lens} tokens, chunk {args.chunk_size}"
@@ -308,7 +317,7 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
         from qwen_infra_b200.vpp.stages import StageBoundaries
 
-        transport = StageBoundaries(rank, world, dev, args.chunk_size, shape.hidden, backend=args.transport,
+        transport = StageBoundaries(rank, world, dev, args.chunk_size, shape.hidden, backend=args.transport[0],
                                     profile=args.profile, resource_layout=args.resource_layout)
     reqs = request_tokens(args)
     runner = FoldedRank(shape, rank, world, dev, reqs, args.chunk_size, transport=transport,
@@ -402,6 +411,38 @@ def run_ours(args):
         e2e = dict(value=tokens / (e2e_ms / 1e3), unit="tok/s", ms_per_step=e2e_ms,
                    h2d_bytes_per_step=tokens * shape.hidden * 2, d2h_bytes_per_step=len(reqs) * 4)
 
+    # --- the second transport, if asked: same ranks, weights and bank ----
+    compare = {}
+    if world > 1 and len(args.transport) > 1:
+        from qwen_infra_b200.vpp.stages import StageBoundaries
+
+        transport.close()
+        transport = StageBoundaries(rank, world, dev, args.chunk_size, shape.hidden, backend=args.transport[1],
+                                    profile=args.profile, resource_layout=args.resource_layout)
+        runner.transport = transport
+        for _ in range(args.warmup):
+            runner.run_bank(embeds)
+        torch.cuda.synchronize()
+        barrier()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        for _ in range(args.steps):
+            runner.run_bank(embeds)
+        c1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        cms = max_over_ranks(c0.elapsed_time(c1) / args.steps)
+        b0.record(stream)
+        runner.run_bank(embeds, record_events=True)
+        b1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        cspan = max_over_ranks(b0.elapsed_time(b1))
+        cbusy = max_over_ranks(runner.compute_ms())
+        runner.model.check_status()
+        compare[args.transport[1]] = dict(ms_per_step=cms, value=sum(reqs) / (cms / 1e3), unit="tok/s",
+                                          bubble_fraction=max(0.0, (cspan - cbusy) / cspan))
+
     if rank != 0:
         if transport is not None:
             transport.close()
@@ -466,7 +507,7 @@ def run_ours(args):
                     model=args.model, layers=shape.layers, requests=len(reqs),
                     prompt_tokens=reqs, chunk=args.chunk_size,
                     virtual_stages=2 * world if args.profile == "vpp" else world,
-                    parallelism=f"folded-vpp pp{world}" if args.profile == "vpp" else f"pp{world}", transport=(args.transport if world > 1 else "local fold"),
+                    parallelism=f"folded-vpp pp{world}" if args.profile == "vpp" else f"pp{world}", transport=(args.transport[0] if world > 1 else "local fold"),
                     stage_streams=2 if runner.overlap else 1, attention=runner.model.attention,
                     l2="inputs larger than L2 (weights ~16 GB, KV pages)"),
         bubble_fraction=bubble, busiest_rank_compute_ms=busiest, instrumented_bank_ms=makespan,
@@ -474,6 +515,8 @@ def run_ours(args):
         gpu_launches=int(launches_per_step * args.steps), kernels=kernels, roofline=roofline, clocks=clocks,
         e2e=e2e, cpu_baseline=cpu,
     )
+    if compare:
+        line["transport_compare"] = compare
     print(json.dumps(line), flush=True)
     if transport is not None:
         transport.close()
