@@ -80,8 +80,12 @@ QI_DEV float block_max(float v, float* scratch32) {
 }
 
 // One CTA per row, thread t owns elements [16t, 16t+16) (= scale group t).
+// The kernel waits on its loads with too few warps (a CTA per row, the block
+// reduction between the loads and the stores), and at 34 registers a thread
+// four 10-warp CTAs fill an SM's register file; capped at 32 (no spills),
+// five do.
 template <bool kQuant>
-__global__ void norm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ residual,
+__global__ void __maxnreg__(32) norm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ residual,
                             const __nv_bfloat16* __restrict__ gamma, const float* __restrict__ gscale,
                             uint8_t* __restrict__ q, uint8_t* __restrict__ sf, __nv_bfloat16* __restrict__ updated,
                             __nv_bfloat16* __restrict__ y_out, int hidden, float eps, float woff) {
