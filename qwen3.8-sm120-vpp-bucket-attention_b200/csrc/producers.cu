@@ -153,6 +153,20 @@ __global__ void __maxnreg__(32) norm_kernel(const __nv_bfloat16* __restrict__ x,
 QI_DEV float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 QI_DEV float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
+QI_DEV void unpack8_bf16(const uint4& a, float* out) {
+  const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    out[2 * i] = bf16_lo(w[i]);
+    out[2 * i + 1] = bf16_hi(w[i]);
+  }
+}
+// Element e (compile-time in unrolled loops) of 8 packed bf16 values.
+QI_DEV float bf16_at(const uint4& a, int e) {
+  const uint32_t w = e < 2 ? a.x : e < 4 ? a.y : e < 6 ? a.z : a.w;
+  return (e & 1) ? bf16_hi(w) : bf16_lo(w);
+}
+
 QI_DEV void load8_bf16(const __nv_bfloat16* p, float* out) {
   const uint4 a = *reinterpret_cast<const uint4*>(p);
   const uint32_t w[4] = {a.x, a.y, a.z, a.w};
@@ -234,8 +248,10 @@ QI_DEV uint32_t kv_quant8(const float* v, float g, uint32_t* scale_code) {
 // (its heads' values, the V values of a K task, cos/sin and its norm weight)
 // is issued before any arithmetic, so each warp has all its bytes in flight
 // at once; only the weights of the task's own kind are held.
+// Capped at 64 registers (three spilled words; 74 uncapped): five 6-warp CTAs
+// per SM instead of four -- the kernel is latency-bound, so warps are speed.
 template <int D>
-__global__ void __launch_bounds__(256) front_kernel(QiFront p) {
+__global__ void __maxnreg__(64) front_kernel(QiFront p) {
   constexpr int HALF = D / 2, L = D / 16, HPW = 32 / L;
   const int lane = threadIdx.x & 31;
   const int sub = lane % L, hsel = lane / L;
@@ -258,32 +274,33 @@ __global__ void __launch_bounds__(256) front_kernel(QiFront p) {
   const int64_t base =
       row * p.input_row + (is_k ? (int64_t)p.qheads * 2 * D + (int64_t)local * D : (int64_t)local * 2 * D);
   const int64_t vbase = row * p.input_row + (int64_t)p.qheads * 2 * D + (int64_t)p.kvheads * D + (int64_t)local * D;
-  float x[8], y[8], vx[8], vy[8];
+  // bf16 operands stay packed (4 registers per 8 values) until they are used:
+  // the kernel is latency-bound, so registers are warps.
+  uint4 xr = make_uint4(0, 0, 0, 0), yr = xr, vxr = xr, vyr = xr;
   if (live) {
-    load8_bf16(qkv + base + d0, x);
-    load8_bf16(qkv + base + HALF + d0, y);
+    xr = *reinterpret_cast<const uint4*>(qkv + base + d0);
+    yr = *reinterpret_cast<const uint4*>(qkv + base + HALF + d0);
     if (is_k) {
-      load8_bf16(qkv + vbase + d0, vx);
-      load8_bf16(qkv + vbase + HALF + d0, vy);
+      vxr = *reinterpret_cast<const uint4*>(qkv + vbase + d0);
+      vyr = *reinterpret_cast<const uint4*>(qkv + vbase + HALF + d0);
     }
-  } else {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) x[e] = y[e] = vx[e] = vy[e] = 0.0f;
   }
   const int64_t pos = p.pos_long ? static_cast<const int64_t*>(p.positions)[row]
                                  : static_cast<const int32_t*>(p.positions)[row];
-  float cs[8], sn[8], w0[8], w1[8];
+  float cs[8], sn[8];
   const __nv_bfloat16* wsrc = static_cast<const __nv_bfloat16*>(is_k ? p.k_weight : p.q_weight);
-  load8_bf16(wsrc + d0, w0);
-  load8_bf16(wsrc + HALF + d0, w1);
+  const uint4 w0r = *reinterpret_cast<const uint4*>(wsrc + d0), w1r = *reinterpret_cast<const uint4*>(wsrc + HALF + d0);
   load8_trig(p.cos_sin, pos * p.cos_row + d0, p.cos_float, cs);
   load8_trig(p.cos_sin, pos * p.cos_row + HALF + d0, p.cos_float, sn);
+  float x[8], y[8];
+  unpack8_bf16(xr, x);
+  unpack8_bf16(yr, y);
   const float total = head_sum_squares<L>(x, y);
   const float inv = rsqrtf(__fadd_rn(__fdiv_rn(total, (float)D), p.eps));  // nvfp4_attention_front.cu:81
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
-    const float a = bf16r(__fmul_rn(__fmul_rn(x[e], inv), __fadd_rn(w0[e], p.weight_offset)));
-    const float b = bf16r(__fmul_rn(__fmul_rn(y[e], inv), __fadd_rn(w1[e], p.weight_offset)));
+    const float a = bf16r(__fmul_rn(__fmul_rn(x[e], inv), __fadd_rn(bf16_at(w0r, e), p.weight_offset)));
+    const float b = bf16r(__fmul_rn(__fmul_rn(y[e], inv), __fadd_rn(bf16_at(w1r, e), p.weight_offset)));
     x[e] = bf16r(__fsub_rn(__fmul_rn(a, cs[e]), __fmul_rn(b, sn[e])));
     y[e] = bf16r(__fadd_rn(__fmul_rn(b, cs[e]), __fmul_rn(a, sn[e])));
   }
@@ -317,6 +334,11 @@ __global__ void __launch_bounds__(256) front_kernel(QiFront p) {
     uint8_t* scales = static_cast<uint8_t*>(which ? p.v_scales : p.k_scales) + sfo;
     uint32_t sx, sy;
     // K: the normed, rotated values; V: the raw projection values
+    float vx[8], vy[8];
+    if (which) {
+      unpack8_bf16(vxr, vx);
+      unpack8_bf16(vyr, vy);
+    }
     const uint32_t cx = kv_quant8(which ? vx : x, which ? vg : kg, &sx);
     const uint32_t cy = kv_quant8(which ? vy : y, which ? vg : kg, &sy);
     if (live) {
@@ -336,7 +358,9 @@ __global__ void __launch_bounds__(256) front_kernel(QiFront p) {
 // [q(D) | gate(D)] blocks (head_dim = D, head_stride = 2D).
 // With static_scale (the reference's form: one per-tensor scale) the row
 // maximum is not taken and scale_out is not written.
-__global__ void gate_fp8_kernel(const __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ gate,
+// Capped at 40 registers (one spilled word): three CTAs of 512 threads per SM
+// instead of two -- the kernel is latency- and XU-bound, so warps are speed.
+__global__ void __maxnreg__(40) gate_fp8_kernel(const __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ gate,
                                 int64_t out_row, int64_t gate_row, int head_dim, int64_t head_stride,
                                 uint8_t* __restrict__ fp8, int64_t fp8_row, float* __restrict__ scale_out, int cols,
                                 const float* __restrict__ static_scale) {
