@@ -236,17 +236,16 @@ typedef struct QiPagedAttention {
 int qi_paged_prefill_attention(const QiPagedAttention* p, cudaStream_t stream);
 
 /* qi_kv_dequant + qi_prefill_attention in one call that allocates nothing, for
- * callers that cannot allocate device memory (inside a graph capture or an
- * allocator callback, or a plugin host that only hands out input and output
- * buffers).  No counterpart in the reference project.  The f16 K / V^T scratch
+ * callers that cannot allocate device memory (an allocator callback, or a
+ * plugin host that only hands out input and output buffers).  No counterpart in the reference project.  The f16 K / V^T scratch
  * lives in a 32 MiB static device array (and the attention split workspace in
  * a second one of about 21 MB) that every GPU loading this library holds until
  * exit; history + rows is limited to what fits (Hkv * D * 4 bytes
  * per token, plus V^T padding to 64 tokens: 8192 tokens for 8 KV heads of 128),
  * larger calls return cudaErrorInvalidValue.  All calls share the array:
  * calls that overlap on the GPU race, so order them on one stream.  The first
- * call on a device looks up the array's device address; make it before any
- * stream capture.  q / out / strides as in QiAttention. */
+ * call on a device looks up the array's device address.  q / out / strides as
+ * in QiAttention. */
 int qi_paged_prefill_attention_noalloc(const QiKvView* kv, const int32_t* block_table, const void* q,
                                        int64_t q_row, void* out, int64_t out_row, int rows, int history,
                                        int qheads, const float* k_global, const float* v_global,

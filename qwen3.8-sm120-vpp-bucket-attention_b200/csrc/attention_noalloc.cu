@@ -2,10 +2,9 @@
 //
 // The regular path (qi_kv_dequant + qi_prefill_attention) needs a caller-
 // provided scratch buffer for the f16 K / V^T it reads.  Some callers cannot
-// call cudaMalloc at that point: code running inside a CUDA-graph capture
-// region or a custom allocator callback, a plugin host that hands out only
-// input/output buffers, or a process whose memory budget is already fully
-// reserved by its framework.  This entry point keeps that scratch in a
+// call cudaMalloc at that point: a custom allocator callback, a plugin host
+// that hands out only input/output buffers, or a process whose memory budget
+// is already fully reserved by its framework.  This entry point keeps that scratch in a
 // fixed, statically sized device array instead, so a call allocates nothing.
 //
 // Cost and limits:
@@ -23,8 +22,7 @@
 //     same call.  The split workspace's arrival counters must start even;
 //     every call clears them first (cudaMemsetAsync, which allocates nothing).
 //   * the first call on a device looks the array's device address up (with
-//     that device current) and caches it; make that first call before any
-//     stream capture.
+//     that device current) and caches it.
 #include <cuda_runtime.h>
 
 #include <mutex>

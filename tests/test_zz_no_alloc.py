@@ -1,6 +1,6 @@
 """The allocation-free paged attention entry point (for callers that cannot
-allocate device memory: graph-capture regions, allocator callbacks, plugin
-hosts that only provide inputs and outputs) must return what the regular
+allocate device memory: allocator callbacks, plugin hosts that only provide
+inputs and outputs) must return what the regular
 two-call path returns.  Called through the C ABI twice in a row with different
 shapes, since every call reuses the same static scratch array.  Collected last
 on purpose (file name), so a failure here comes after every other test ran."""
