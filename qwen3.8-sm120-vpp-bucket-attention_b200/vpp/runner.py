@@ -102,6 +102,70 @@ class FoldedRank:
             self.contexts = [self.model.chunk_context(c.request, c.start, c.rows) for c in self.chunks]
         return self.contexts
 
+    def run_op(self, batch, stage, embeds=None, host_embeds=None, *, record_events=False):
+        """One op of this rank's order, on the current stream: receive (or the
+        local fold, or the chunk's embeddings on stage 0) -> the stage's
+        layers -> send -> retire; on the last stage the final norm of a
+        request's last row.  ``run_bank`` runs its serial path as these ops in
+        ``self.order``; ``vpp.worker.FoldedWorker`` runs them one step at a
+        time (the transport's grant order must then be ``self.order``)."""
+        G = self.ranks
+        last_stage = self.stage_count - 1
+        folded = self.profile == "vpp"
+        ch = self.chunks[batch]
+        ctx = self._contexts()[batch]
+        stream = torch.cuda.current_stream(self.device)
+        if stage == 0:
+            if host_embeds is not None:
+                hidden = host_embeds[ch.request][ch.start:ch.start + ch.rows].to(self.device, non_blocking=True)
+            else:
+                hidden = embeds[ch.request][ch.start:ch.start + ch.rows]
+            residual = None
+        elif folded and stage == G:  # local fold: stage G-1 ran on this rank just before
+            hidden, residual = self.fold[0][:ch.rows], self.fold[1][:ch.rows]
+        else:
+            hidden, residual = self.transport.receive(batch, stage, ch.rows)
+        if record_events:  # after the input is ready: stage time excludes waiting
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev0.record(stream)
+        span = (L.stage_layers(stage, G, self.shape.layers) if folded
+                else L.cpp_layer_range(stage, G, self.shape.layers))
+        on_residual = None
+        if folded and stage == G - 1:
+            out_planes = (self.fold[0][:ch.rows], self.fold[1][:ch.rows])
+        elif stage == last_stage:
+            out_planes = None
+        else:
+            out_planes = self.transport.prepare_send(batch, stage, ch.rows)
+            on_residual = (lambda b=batch, s=stage: self.transport.mark_residual_ready(b, s))
+        h, r = self.model.run_layers(span, hidden, residual, ctx, out_planes, on_residual)
+        if stage != last_stage and not (folded and stage == G - 1):
+            self.transport.send(batch, stage, ch.rows)
+        if stage != 0 and not (folded and stage == G):
+            self.transport.retire(batch, stage)
+        if stage == last_stage:
+            if self.keep_all_outputs:
+                self.outputs[batch] = self.model.final_norm(h, r)
+            if ch.start + ch.rows == self.request_tokens[ch.request]:
+                self.model.final_norm(h[-1:], r[-1:], out=self.last_hidden[ch.request:ch.request + 1])
+        if record_events:
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev1.record(stream)
+            self.stage_events.append((batch, stage, ev0, ev1))
+
+    def sample(self, requests=None):
+        """P+1 on the output rank: the greedy token of each request in
+        ``requests`` (all by default) from its final-normed last row, into
+        ``last_tokens``."""
+        if self.rank != self.output_rank:
+            raise RuntimeError("only the output rank samples")
+        if requests is None:
+            self.model.sample(self.last_hidden, tokens=self.last_tokens)
+        else:
+            for q in requests:
+                self.model.sample(self.last_hidden[q:q + 1], tokens=self.last_tokens[q:q + 1])
+        return self.last_tokens
+
     def run_bank(self, embeds, *, host_embeds=None, record_events=False):
         """Run this rank's ops for one bank.  ``embeds``: device bf16 [tokens, H]
         per request (list), or None with ``host_embeds`` (pinned host tensors,
@@ -111,54 +175,11 @@ class FoldedRank:
         device times) runs the stages in series on the current stream."""
         if self.overlap and not record_events:
             return self._run_bank_overlapped(embeds, host_embeds)
-        G = self.ranks
-        last_stage = self.stage_count - 1
-        folded = self.profile == "vpp"
-        ctxs = self._contexts()
-        stream = torch.cuda.current_stream(self.device)
         self.stage_events = []
         if self.transport is not None:
             self.transport.set_order(self.order)
         for batch, stage in self.order:
-            ch = self.chunks[batch]
-            ctx = ctxs[batch]
-            if stage == 0:
-                if host_embeds is not None:
-                    hidden = host_embeds[ch.request][ch.start:ch.start + ch.rows].to(self.device, non_blocking=True)
-                else:
-                    hidden = embeds[ch.request][ch.start:ch.start + ch.rows]
-                residual = None
-            elif folded and stage == G:  # local fold: stage G-1 ran on this rank just before
-                hidden, residual = self.fold[0][:ch.rows], self.fold[1][:ch.rows]
-            else:
-                hidden, residual = self.transport.receive(batch, stage, ch.rows)
-            if record_events:  # after the input is ready: stage time excludes waiting
-                ev0 = torch.cuda.Event(enable_timing=True)
-                ev0.record(stream)
-            span = (L.stage_layers(stage, G, self.shape.layers) if folded
-                    else L.cpp_layer_range(stage, G, self.shape.layers))
-            on_residual = None
-            if folded and stage == G - 1:
-                out_planes = (self.fold[0][:ch.rows], self.fold[1][:ch.rows])
-            elif stage == last_stage:
-                out_planes = None
-            else:
-                out_planes = self.transport.prepare_send(batch, stage, ch.rows)
-                on_residual = (lambda b=batch, s=stage: self.transport.mark_residual_ready(b, s))
-            h, r = self.model.run_layers(span, hidden, residual, ctx, out_planes, on_residual)
-            if stage != last_stage and not (folded and stage == G - 1):
-                self.transport.send(batch, stage, ch.rows)
-            if stage != 0 and not (folded and stage == G):
-                self.transport.retire(batch, stage)
-            if stage == last_stage:
-                if self.keep_all_outputs:
-                    self.outputs[batch] = self.model.final_norm(h, r)
-                if ch.start + ch.rows == self.request_tokens[ch.request]:
-                    self.model.final_norm(h[-1:], r[-1:], out=self.last_hidden[ch.request:ch.request + 1])
-            if record_events:
-                ev1 = torch.cuda.Event(enable_timing=True)
-                ev1.record(stream)
-                self.stage_events.append((batch, stage, ev0, ev1))
+            self.run_op(batch, stage, embeds, host_embeds, record_events=record_events)
         if self.rank == self.output_rank:
             # P+1: the one output token of every request (greedy), part of the bank.
             self.model.sample(self.last_hidden, tokens=self.last_tokens)
