@@ -471,17 +471,21 @@ def run_ours(args):
     if kernels:
         dom_name = max(kernels, key=lambda n: kernels[n]["ms_per_step"])
         dom = kernels[dom_name]
+        # The bank's kernels are timed inside a seconds-long step under the
+        # power cap, so the tensor denominators are the sustained bf16 figure.
+        tensor, tkey = (peaks["bf16_tflops_sustained"], "bf16_tflops_sustained") \
+            if "bf16_tflops_sustained" in peaks else (peaks["bf16_tflops"], "bf16_tflops")
         if dom["unit"] == "GB/s":
             peak, pk = peaks["hbm_gbs"], f"hbm_gbs ({peak_kind})"
             bound = "hbm"
         elif dom_name == "gemm_nvfp4":
-            peak, pk = 4 * peaks["bf16_tflops"], f"4 x bf16_tflops ({peak_kind}; dense NVFP4:BF16 = 4:1 nominal)"
+            peak, pk = 4 * tensor, f"4 x {tkey} ({peak_kind}; dense NVFP4:BF16 = 4:1 nominal)"
             bound = "tensor"
         elif dom_name == "gemm_e4m3":
-            peak, pk = 2 * peaks["bf16_tflops"], f"2 x bf16_tflops ({peak_kind}; dense FP8:BF16 = 2:1 nominal)"
+            peak, pk = 2 * tensor, f"2 x {tkey} ({peak_kind}; dense FP8:BF16 = 2:1 nominal)"
             bound = "tensor"
         else:
-            peak, pk = peaks["bf16_tflops"], f"bf16_tflops ({peak_kind})"
+            peak, pk = tensor, f"{tkey} ({peak_kind})"
             bound = "tensor"
         traffic = traffic_source = None
         if dom_name == "attention" and args.model == "qwen27b" and args.chunk_size == ATTN_TRAFFIC_ROWS:
